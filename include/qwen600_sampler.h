@@ -1,0 +1,166 @@
+/*
+ * qwen600_sampler.h — C ABI of the B200 token sampler.
+ *
+ * A drop-in for the host sampler of KennethWang1221/qwen600_engine
+ * (sampler.h): same parameters (temperature, top-k, top-p, min-p,
+ * repetition / frequency / presence penalty over a token window, seeded
+ * xorshift64*), same results on the same logits, history and RNG states,
+ * computed by sm_100a CUDA kernels on device-resident logits.
+ *
+ * Conventions
+ *  - Every function returns an int status: QS_OK (0) or a negative QS_ERR_*.
+ *    Nothing here calls exit() (the reference does on allocation failure,
+ *    sampler.h:298-317).  qs_last_error() gives a message for the calling
+ *    thread.
+ *  - Device pointers are owned by the caller and used on the caller's
+ *    stream.  The library allocates device memory only in qs_build_sampler
+ *    (workspace and per-row state sized for max_batch × vocab); sampling
+ *    calls allocate nothing.
+ *  - Logits are read only, unless QS_FLAG_WRITE_PENALIZED is set on an fp32
+ *    call: then the penalised values are written back in place, as the
+ *    reference's sample() does (sampler.h:125-138).
+ *  - A handle may be used from one stream at a time; different handles are
+ *    independent.
+ *
+ * RNG contract: row r has its own xorshift64* state (sampler.h:49-60),
+ * advanced once per non-greedy draw exactly as random_f32.  Handles seeded
+ * with `seed` give row r the state seed + r.
+ */
+#ifndef QWEN600_SAMPLER_H
+#define QWEN600_SAMPLER_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QS_API __attribute__((visibility("default")))
+#else
+#define QS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QS_OK 0
+#define QS_ERR_INVALID (-1)     /* bad argument (NULL, size, dtype, range) */
+#define QS_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define QS_ERR_ALLOC (-3)       /* device or host allocation failed */
+#define QS_ERR_UNSUPPORTED (-4) /* valid request outside this build's limits */
+
+typedef enum { QS_F32 = 0, QS_BF16 = 1 } qs_dtype;
+
+/* Bit flags for the sampling calls. */
+#define QS_FLAG_WRITE_PENALIZED 1u /* fp32 only: write penalised logits back */
+#define QS_FLAG_INDEX_TIES 2u      /* order equal probabilities by token id
+                                      instead of reproducing the reference's
+                                      quick_select arrangement (faster, not
+                                      reference-identical on ties) */
+
+/* Sampling parameters; field meanings as the reference Sampler's
+ * (sampler.h:23-31).  top_k <= 0 or >= vocab means "no top-k" (full sort,
+ * sampler.h:212-218). temperature < 1e-6 means greedy (sampler.h:178). */
+typedef struct {
+    float temperature;
+    float topp;
+    float minp;
+    int top_k;
+    float repetition_penalty;
+    float frequency_penalty;
+    float presence_penalty;
+} qs_params;
+
+/* Per-row diagnostics written by qs_sample_rows_debug (device memory). */
+typedef struct {
+    int token;        /* sampled id */
+    int greedy;       /* 1 if the argmax branch was taken */
+    int n_topk;       /* candidates after top-k (sampler.h:209-218) */
+    int n_minp;       /* after min-p (sampler.h:221-223) */
+    int n_final;      /* after top-p (sampler.h:226-237) */
+    int draw_pos;     /* position of the drawn candidate in the final order */
+    int exact_ties;   /* 1 if the reference tie order had to be reproduced */
+    int sum_fallback; /* exact-sum segments evaluated element by element */
+    float max_logit;  /* max of the temperature-scaled logits */
+    float sum;        /* softmax denominator, bit-identical to sampler.h:195-201 */
+    float r;          /* the uniform drawn (sampler.h:246) */
+    float renorm_sum; /* sampler.h:240-241 */
+} qs_row_debug;
+
+typedef struct qs_sampler qs_sampler;
+
+/* build_sampler (sampler.h:277-327), batched: a handle for up to max_batch
+ * rows over `vocab` tokens with a `penalty_window`-slot history per row
+ * (0 = no history), on CUDA device `device`.  Row r's RNG state = seed + r. */
+QS_API int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch,
+                     int vocab, int penalty_window, unsigned long long seed,
+                     int device);
+
+/* free_sampler (sampler.h:330-343). NULL is accepted. */
+QS_API int qs_free_sampler(qs_sampler* s);
+
+/* Replaces the direct Sampler field writes of python/bindings.cu:213-235. */
+QS_API int qs_set_params(qs_sampler* s, const qs_params* params);
+QS_API int qs_get_params(const qs_sampler* s, qs_params* out);
+
+/* Set / read the per-row RNG states (bindings.cu:236-238 sets rng_state). */
+QS_API int qs_set_rng_state(qs_sampler* s, const unsigned long long* host_states, int n);
+QS_API int qs_get_rng_state(qs_sampler* s, unsigned long long* host_states, int n);
+
+/* reset_sampler_history (sampler.h:346-354): clears every row's window and
+ * cumulative token counts (enqueued on the handle's default stream, then
+ * synchronised). */
+QS_API int qs_reset_sampler_history(qs_sampler* s);
+
+/* sample() (sampler.h:165-270), batched and stateful: rows [0, batch) of
+ * d_logits ([batch, vocab], row-major, fp32 or bf16) are penalised from the
+ * handle's device-resident history, sampled, and each row's history and
+ * token counts are updated with its token (sampler.h:257-267).
+ * d_tokens: [batch] int32 device output.  stream: a cudaStream_t (NULL = the
+ * legacy default stream). */
+QS_API int qs_sample(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch,
+              int* d_tokens, void* stream, unsigned flags);
+
+/* Stateless batched sampling with caller-supplied history: the same
+ * computation as sample() per row, where row r's window is
+ * d_hist[r*window + i] for i < d_hist_count[r] (ring storage order, as
+ * sampler.h:118 iterates it) and d_hist_counts[r*window + i] is
+ * token_counts[d_hist[...]] (NULL: all zero).  d_rng: [batch] states, advanced
+ * in place.  The handle supplies workspace only; its own history and RNG
+ * states are untouched.  window must not exceed the handle's window
+ * (or 1024 when the handle has none). */
+QS_API int qs_sample_rows(qs_sampler* s, const void* d_logits, qs_dtype dtype,
+                   int batch, int vocab, const int* d_hist,
+                   const float* d_hist_counts, const int* d_hist_count,
+                   int window, unsigned long long* d_rng, int* d_tokens,
+                   void* stream, unsigned flags);
+
+/* qs_sample_rows plus diagnostics: d_debug [batch] (may be NULL),
+ * d_probs [batch, vocab] fp32 normalised softmax in token order
+ * (sampler.h:204-207; may be NULL), d_cand_index / d_cand_prob
+ * [batch, cand_cap]: the final candidate order after renormalisation
+ * (may be NULL). */
+QS_API int qs_sample_rows_debug(qs_sampler* s, const void* d_logits, qs_dtype dtype,
+                         int batch, int vocab, const int* d_hist,
+                         const float* d_hist_counts, const int* d_hist_count,
+                         int window, unsigned long long* d_rng, int* d_tokens,
+                         qs_row_debug* d_debug, float* d_probs,
+                         int* d_cand_index, float* d_cand_prob, int cand_cap,
+                         void* stream, unsigned flags);
+
+/* Host-buffer entry, the shape of the reference's sample(Sampler*, float*)
+ * for callers that still hold logits on the host (bindings.cu:170,
+ * main.cu:139): copies h_logits ([batch, vocab] fp32) to the device, runs
+ * qs_sample on the handle's stream, copies the tokens back to h_tokens and
+ * synchronises. */
+QS_API int qs_sample_host(qs_sampler* s, const float* h_logits, int batch, int* h_tokens,
+                   unsigned flags);
+
+/* Message for the last error on the calling thread ("" if none). */
+QS_API const char* qs_last_error(void);
+
+/* Library limits. */
+QS_API int qs_max_vocab(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN600_SAMPLER_H */

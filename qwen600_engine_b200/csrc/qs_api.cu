@@ -1,0 +1,440 @@
+// C ABI of the B200 sampler (include/qwen600_sampler.h): handle lifetime,
+// parameter / RNG / history management and the launch sequence
+//   penalty_kernel -> row_kernel -> ties_kernel -> emit_kernel
+// on the caller's stream.  All device memory is allocated in
+// qs_build_sampler; the sampling entry points allocate nothing.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <new>
+#include <string>
+#include <vector>
+
+#include "qs_common.cuh"
+#include "qwen600_sampler.h"
+
+namespace qs {
+
+template <typename T>
+cudaError_t launch_penalty(const T*, int, int, const int*, int, const int*, const float*,
+                          const float*, float, float, float, int*, int*, float*, int, float*,
+                          cudaStream_t);
+
+size_t row_kernel_smem(int V, int dtype_bytes, int ov_stride);
+template <typename T>
+cudaError_t launch_row_kernel(const T*, int, int, RowParams, const int*, const int*, const float*,
+                              int, unsigned long long*, RowResult*, int*, int*, int*, float*, int,
+                              cudaStream_t);
+template <typename T>
+cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
+                               const int*, const int*, RowResult*, unsigned long long*, int*, int,
+                               int*, float*, int, cudaStream_t);
+cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
+                        float*, cudaStream_t);
+template <typename T>
+cudaError_t launch_probs(const T*, int, int, const int*, const int*, const float*, int,
+                         const RowResult*, float*, cudaStream_t);
+
+}  // namespace qs
+
+using namespace qs;
+
+static thread_local std::string g_err;
+
+static int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                        \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return fail(QS_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_),   \
+                        __FILE__, __LINE__);                                            \
+    } while (0)
+
+struct qs_sampler {
+    int device = 0;
+    int max_batch = 0;
+    int vocab = 0;
+    int window = 0;     // history slots per row held by the handle
+    int ov_stride = 0;  // override table capacity per row
+    int tie_ctas = 0;
+    qs_params params{};
+    cudaStream_t stream = nullptr;
+    // workspace
+    int* ov_n = nullptr;
+    int* ov_idx = nullptr;
+    float* ov_val = nullptr;
+    RowResult* res = nullptr;
+    int* slow_list = nullptr;
+    int* slow_count = nullptr;
+    unsigned long long* tie_scratch = nullptr;
+    int* tie_pos = nullptr;
+    // per-row state of the stateful API (sampler.h:33-41)
+    int* ring = nullptr;
+    int* hcount = nullptr;
+    int* hpos = nullptr;
+    float* token_counts = nullptr;
+    unsigned long long* rng = nullptr;
+    // host-entry staging
+    float* d_in = nullptr;
+    int* d_tok = nullptr;
+};
+
+static void release(qs_sampler* s) {
+    if (!s) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(s->device);
+    void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
+                    s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts,
+                    s->rng, s->d_in, s->d_tok};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    if (s->stream) cudaStreamDestroy(s->stream);
+    cudaSetDevice(prev);
+    delete s;
+}
+
+static int check_params(const qs_params* p) {
+    if (!p) return fail(QS_ERR_INVALID, "params is NULL");
+    if (p->repetition_penalty == 0.0f)
+        return fail(QS_ERR_INVALID, "repetition_penalty must be nonzero");
+    return QS_OK;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+extern "C" {
+
+const char* qs_last_error(void) { return g_err.c_str(); }
+
+int qs_max_vocab(void) { return kMaxVocab; }
+
+int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, int vocab,
+                     int penalty_window, unsigned long long seed, int device) {
+    g_err.clear();
+    if (!out) return fail(QS_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    int rc = check_params(params);
+    if (rc) return rc;
+    if (max_batch < 1) return fail(QS_ERR_INVALID, "max_batch must be >= 1");
+    if (vocab < 1 || vocab > kMaxVocab)
+        return fail(QS_ERR_UNSUPPORTED, "vocab %d outside [1, %d]", vocab, kMaxVocab);
+    if (penalty_window < 0 || penalty_window > kMaxWindow)
+        return fail(QS_ERR_UNSUPPORTED, "penalty_window %d outside [0, %d]", penalty_window,
+                    kMaxWindow);
+    int ndev = 0;
+    CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(QS_ERR_INVALID, "device %d not present", device);
+    DeviceGuard dg(device);
+    qs_sampler* s = new (std::nothrow) qs_sampler();
+    if (!s) return fail(QS_ERR_ALLOC, "host allocation failed");
+    s->device = device;
+    s->max_batch = max_batch;
+    s->vocab = vocab;
+    s->window = penalty_window;
+    s->ov_stride = penalty_window > 0 ? penalty_window : 1024;
+    s->params = *params;
+    s->tie_ctas = max_batch < 148 ? max_batch : 148;
+    const size_t B = (size_t)max_batch, V = (size_t)vocab, W = (size_t)penalty_window;
+#define ALLOC(ptr, bytes)                                                                  \
+    do {                                                                                   \
+        cudaError_t e_ = cudaMalloc((void**)&(ptr), (bytes) > 0 ? (bytes) : 16);           \
+        if (e_ != cudaSuccess) {                                                           \
+            release(s);                                                                    \
+            return fail(QS_ERR_ALLOC, "cudaMalloc(%zu) failed: %s", (size_t)(bytes),       \
+                        cudaGetErrorString(e_));                                           \
+        }                                                                                  \
+    } while (0)
+    ALLOC(s->ov_n, sizeof(int) * B);
+    ALLOC(s->ov_idx, sizeof(int) * B * s->ov_stride);
+    ALLOC(s->ov_val, sizeof(float) * B * s->ov_stride);
+    ALLOC(s->res, sizeof(RowResult) * B);
+    ALLOC(s->slow_list, sizeof(int) * B);
+    ALLOC(s->slow_count, sizeof(int));
+    ALLOC(s->tie_scratch, sizeof(unsigned long long) * V * s->tie_ctas);
+    ALLOC(s->tie_pos, sizeof(int) * 2 * V * s->tie_ctas);
+    ALLOC(s->rng, sizeof(unsigned long long) * B);
+    ALLOC(s->d_in, sizeof(float) * B * V);
+    ALLOC(s->d_tok, sizeof(int) * B);
+    if (W > 0) {
+        ALLOC(s->ring, sizeof(int) * B * W);
+        ALLOC(s->hcount, sizeof(int) * B);
+        ALLOC(s->hpos, sizeof(int) * B);
+        ALLOC(s->token_counts, sizeof(float) * B * V);
+    }
+#undef ALLOC
+    cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        release(s);
+        return fail(QS_ERR_CUDA, "cudaStreamCreate: %s", cudaGetErrorString(e));
+    }
+    std::vector<unsigned long long> st(B);
+    for (size_t r = 0; r < B; r++) st[r] = seed + r;
+    e = cudaMemcpy(s->rng, st.data(), sizeof(unsigned long long) * B, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && W > 0) {
+        e = cudaMemset(s->hcount, 0, sizeof(int) * B);
+        if (e == cudaSuccess) e = cudaMemset(s->hpos, 0, sizeof(int) * B);
+        if (e == cudaSuccess) e = cudaMemset(s->token_counts, 0, sizeof(float) * B * V);
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        release(s);
+        return fail(QS_ERR_CUDA, "initialising state: %s", cudaGetErrorString(e));
+    }
+    *out = s;
+    return QS_OK;
+}
+
+int qs_free_sampler(qs_sampler* s) {
+    g_err.clear();
+    if (!s) return QS_OK;
+    {
+        DeviceGuard dg(s->device);
+        cudaStreamSynchronize(s->stream);
+    }
+    release(s);
+    return QS_OK;
+}
+
+int qs_set_params(qs_sampler* s, const qs_params* params) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    int rc = check_params(params);
+    if (rc) return rc;
+    s->params = *params;
+    return QS_OK;
+}
+
+int qs_get_params(const qs_sampler* s, qs_params* out) {
+    g_err.clear();
+    if (!s || !out) return fail(QS_ERR_INVALID, "NULL argument");
+    *out = s->params;
+    return QS_OK;
+}
+
+int qs_set_rng_state(qs_sampler* s, const unsigned long long* host_states, int n) {
+    g_err.clear();
+    if (!s || !host_states) return fail(QS_ERR_INVALID, "NULL argument");
+    if (n < 0 || n > s->max_batch) return fail(QS_ERR_INVALID, "n %d outside [0, %d]", n, s->max_batch);
+    DeviceGuard dg(s->device);
+    CK(cudaMemcpyAsync(s->rng, host_states, sizeof(unsigned long long) * n, cudaMemcpyHostToDevice,
+                       s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+    return QS_OK;
+}
+
+int qs_get_rng_state(qs_sampler* s, unsigned long long* host_states, int n) {
+    g_err.clear();
+    if (!s || !host_states) return fail(QS_ERR_INVALID, "NULL argument");
+    if (n < 0 || n > s->max_batch) return fail(QS_ERR_INVALID, "n %d outside [0, %d]", n, s->max_batch);
+    DeviceGuard dg(s->device);
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(host_states, s->rng, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost));
+    return QS_OK;
+}
+
+int qs_reset_sampler_history(qs_sampler* s) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    if (s->window == 0) return QS_OK;  // no history kept (sampler.h:346-354)
+    DeviceGuard dg(s->device);
+    const size_t B = (size_t)s->max_batch;
+    CK(cudaMemsetAsync(s->hcount, 0, sizeof(int) * B, s->stream));
+    CK(cudaMemsetAsync(s->hpos, 0, sizeof(int) * B, s->stream));
+    CK(cudaMemsetAsync(s->token_counts, 0, sizeof(float) * B * s->vocab, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+    return QS_OK;
+}
+
+}  // extern "C"
+
+// Shared launch sequence of the sampling entry points.
+struct Call {
+    const void* logits;
+    qs_dtype dtype;
+    int batch, vocab;
+    const int* hist;
+    int hist_stride;
+    const int* hist_count;
+    const float* slot_counts;
+    const float* dense_counts;
+    unsigned long long* rng;
+    int* tokens;
+    qs_row_debug* dbg;
+    float* probs;
+    int* cand_index;
+    float* cand_prob;
+    int cand_cap;
+    int* ring;
+    int* hcount;
+    int* hpos;
+    float* token_counts;  // history update target (stateful)
+    cudaStream_t stream;
+    unsigned flags;
+};
+
+static int run(qs_sampler* s, const Call& c) {
+    const qs_params& p = s->params;
+    if (c.dtype != QS_F32 && c.dtype != QS_BF16) return fail(QS_ERR_INVALID, "unknown dtype %d", c.dtype);
+    if (!c.logits || !c.tokens || !c.rng) return fail(QS_ERR_INVALID, "NULL device pointer");
+    if (c.batch < 0 || c.batch > s->max_batch)
+        return fail(QS_ERR_INVALID, "batch %d outside [0, %d]", c.batch, s->max_batch);
+    if (c.vocab != s->vocab) return fail(QS_ERR_INVALID, "vocab %d != handle vocab %d", c.vocab, s->vocab);
+    if ((c.flags & QS_FLAG_WRITE_PENALIZED) && c.dtype != QS_F32)
+        return fail(QS_ERR_INVALID, "QS_FLAG_WRITE_PENALIZED needs fp32 logits");
+    if (c.batch == 0) return QS_OK;
+    const bool greedy = p.temperature < 1e-6f;
+    const bool topk = p.top_k > 0 && p.top_k < c.vocab;
+    if (!greedy && topk && p.top_k > kCandCap / 2)
+        return fail(QS_ERR_UNSUPPORTED, "top_k %d above this build's limit %d", p.top_k, kCandCap / 2);
+    DeviceGuard dg(s->device);
+    const int B = c.batch, V = c.vocab;
+    const bool penalties = c.hist && c.hist_stride > 0 &&
+                           (p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f ||
+                            p.presence_penalty != 0.0f);
+    if (penalties) {
+        float* wb = (c.flags & QS_FLAG_WRITE_PENALIZED) ? (float*)c.logits : nullptr;
+        if (c.dtype == QS_F32) {
+            CK(launch_penalty<float>((const float*)c.logits, B, V, c.hist, c.hist_stride,
+                                     c.hist_count, c.slot_counts, c.dense_counts,
+                                     p.repetition_penalty, p.frequency_penalty, p.presence_penalty,
+                                     s->ov_n, s->ov_idx, s->ov_val, s->ov_stride, wb, c.stream));
+        } else {
+            CK(launch_penalty<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, c.hist,
+                                             c.hist_stride, c.hist_count, c.slot_counts,
+                                             c.dense_counts, p.repetition_penalty,
+                                             p.frequency_penalty, p.presence_penalty, s->ov_n,
+                                             s->ov_idx, s->ov_val, s->ov_stride, nullptr,
+                                             c.stream));
+        }
+    }
+    const int* ovn = penalties ? s->ov_n : nullptr;
+    CK(cudaMemsetAsync(s->slow_count, 0, sizeof(int), c.stream));
+    RowParams rp{p.temperature, p.topp, p.minp, p.top_k, c.flags};
+    if (c.dtype == QS_F32) {
+        CK(launch_row_kernel<float>((const float*)c.logits, B, V, rp, ovn, s->ov_idx, s->ov_val,
+                                    s->ov_stride, c.rng, s->res, s->slow_list, s->slow_count,
+                                    c.cand_index, c.cand_prob, c.cand_cap, c.stream));
+    } else {
+        CK(launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, ovn,
+                                            s->ov_idx, s->ov_val, s->ov_stride, c.rng, s->res,
+                                            s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
+                                            c.cand_cap, c.stream));
+    }
+    if (!greedy && topk && !(c.flags & QS_FLAG_INDEX_TIES)) {
+        TieParams tp{p.temperature, p.topp, p.minp, p.top_k};
+        const int nct = B < s->tie_ctas ? B : s->tie_ctas;
+        if (c.dtype == QS_F32) {
+            CK(launch_ties_kernel<float>((const float*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val,
+                                         s->ov_stride, s->slow_list, s->slow_count, s->res,
+                                         s->tie_scratch, s->tie_pos, nct, c.cand_index, c.cand_prob,
+                                         c.cand_cap, c.stream));
+        } else {
+            CK(launch_ties_kernel<__nv_bfloat16>(
+                (const __nv_bfloat16*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val, s->ov_stride,
+                s->slow_list, s->slow_count, s->res, s->tie_scratch, s->tie_pos, nct, c.cand_index,
+                c.cand_prob, c.cand_cap, c.stream));
+        }
+    }
+    if (c.probs) {
+        if (c.dtype == QS_F32)
+            CK(launch_probs<float>((const float*)c.logits, B, V, ovn, s->ov_idx, s->ov_val,
+                                   s->ov_stride, s->res, c.probs, c.stream));
+        else
+            CK(launch_probs<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, ovn, s->ov_idx,
+                                           s->ov_val, s->ov_stride, s->res, c.probs, c.stream));
+    }
+    CK(launch_emit(B, V, s->window, s->res, c.tokens, c.dbg, c.ring, c.hcount, c.hpos,
+                   c.token_counts, c.stream));
+    return QS_OK;
+}
+
+extern "C" {
+
+int qs_sample(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, int* d_tokens,
+              void* stream, unsigned flags) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    Call c{};
+    c.logits = d_logits; c.dtype = dtype; c.batch = batch; c.vocab = s->vocab;
+    c.hist = s->ring; c.hist_stride = s->window; c.hist_count = s->hcount;
+    c.dense_counts = s->token_counts;
+    c.rng = s->rng; c.tokens = d_tokens;
+    c.ring = s->ring; c.hcount = s->hcount; c.hpos = s->hpos; c.token_counts = s->token_counts;
+    c.stream = (cudaStream_t)stream; c.flags = flags;
+    return run(s, c);
+}
+
+int qs_sample_rows_debug(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, int vocab,
+                         const int* d_hist, const float* d_hist_counts, const int* d_hist_count,
+                         int window, unsigned long long* d_rng, int* d_tokens,
+                         qs_row_debug* d_debug, float* d_probs, int* d_cand_index,
+                         float* d_cand_prob, int cand_cap, void* stream, unsigned flags) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    if (window < 0 || window > s->ov_stride)
+        return fail(QS_ERR_INVALID, "window %d outside [0, %d]", window, s->ov_stride);
+    if (window > 0 && (!d_hist || !d_hist_count))
+        return fail(QS_ERR_INVALID, "window > 0 needs d_hist and d_hist_count");
+    if ((d_cand_index == nullptr) != (d_cand_prob == nullptr) || (d_cand_index && cand_cap < 1))
+        return fail(QS_ERR_INVALID, "candidate outputs need both buffers and cand_cap >= 1");
+    Call c{};
+    c.logits = d_logits; c.dtype = dtype; c.batch = batch; c.vocab = vocab;
+    c.hist = window > 0 ? d_hist : nullptr; c.hist_stride = window; c.hist_count = d_hist_count;
+    c.slot_counts = d_hist_counts;
+    c.rng = d_rng; c.tokens = d_tokens; c.dbg = d_debug; c.probs = d_probs;
+    c.cand_index = d_cand_index; c.cand_prob = d_cand_prob; c.cand_cap = cand_cap;
+    c.stream = (cudaStream_t)stream; c.flags = flags;
+    return run(s, c);
+}
+
+int qs_sample_rows(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, int vocab,
+                   const int* d_hist, const float* d_hist_counts, const int* d_hist_count,
+                   int window, unsigned long long* d_rng, int* d_tokens, void* stream,
+                   unsigned flags) {
+    return qs_sample_rows_debug(s, d_logits, dtype, batch, vocab, d_hist, d_hist_counts,
+                                d_hist_count, window, d_rng, d_tokens, nullptr, nullptr, nullptr,
+                                nullptr, 0, stream, flags);
+}
+
+int qs_sample_host(qs_sampler* s, const float* h_logits, int batch, int* h_tokens, unsigned flags) {
+    g_err.clear();
+    if (!s || !h_logits || !h_tokens) return fail(QS_ERR_INVALID, "NULL argument");
+    if (batch < 0 || batch > s->max_batch)
+        return fail(QS_ERR_INVALID, "batch %d outside [0, %d]", batch, s->max_batch);
+    DeviceGuard dg(s->device);
+    CK(cudaMemcpyAsync(s->d_in, h_logits, sizeof(float) * (size_t)batch * s->vocab,
+                       cudaMemcpyHostToDevice, s->stream));
+    int rc = qs_sample(s, s->d_in, QS_F32, batch, s->d_tok, s->stream, flags);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(h_tokens, s->d_tok, sizeof(int) * (size_t)batch, cudaMemcpyDeviceToHost,
+                       s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+    return QS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,383 @@
+// Exact pass for rows whose sampled identity depends on how the reference
+// orders equal probabilities.
+//
+// The reference selects the top k with a Hoare-partition quick_select that
+// re-reads its pivot at position k-1 every round and stops both scans on
+// equality (sampler.h:75-94), then sorts those k with glibc's stable qsort
+// (sampler.h:214).  Among equal probabilities the result is an arrangement
+// left by the partition swaps, so this pass materialises the row's
+// (probability, index) array exactly as sample() builds it
+// (sampler.h:196-207) and replays every partition round with a parallel,
+// bit-identical formulation of the serial scans:
+//
+//   L = positions whose value <= pivot (where the left scan stops), ascending
+//   R = positions whose value >= pivot (where the right scan stops), descending
+//   swap t exchanges L[t] and R[t] while L[t] <= R[t]; an element at q with
+//   inclusive ranks a(q) = #L in [lo, q], b(q) = #R in [q, hi] is swapped as
+//   an L iff b(q) >= a(q) and as an R iff a(q) >= b(q)
+//
+// and the scans' final i / j follow from the last swap (see partition_round).
+// Then the reference's min-p / top-p / renormalise / draw run on the exact
+// order, with the uniform the row kernel already drew.
+#include "qs_common.cuh"
+
+namespace qs {
+
+constexpr int kTieThreads = 1024;
+constexpr int kTieWarps = kTieThreads / 32;
+
+__device__ __forceinline__ int tie_excl_scan(int v, int* red, int* total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    __syncthreads();
+    if (lane == 31) red[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int s = lane < kTieWarps ? red[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        if (lane < kTieWarps) red[lane] = s;
+    }
+    __syncthreads();
+    int before = (w == 0) ? 0 : red[w - 1];
+    *total = red[kTieWarps - 1];
+    return before + x - v;
+}
+
+__device__ __forceinline__ int tie_sum(int v, int* red) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    int r = lane < kTieWarps ? red[lane] : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+}
+
+__device__ __forceinline__ uint32_t pbits(unsigned long long a) { return (uint32_t)(a >> 32); }
+
+// One round of the reference's partition loop on A[lo..hi] with pivot bits P.
+// Returns the scans' final (i, j) in *oi / *oj (valid in every thread).
+__device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t P, int* posL,
+                                int* posR, int* red, int* sh, int* oi, int* oj) {
+    const int tid = threadIdx.x;
+    const int n = hi - lo + 1;
+    const int per = (n + kTieThreads - 1) / kTieThreads;
+    const int c0 = lo + tid * per;
+    const int c1 = min(c0 + per, hi + 1);
+    int cl = 0, cr = 0;
+    for (int q = c0; q < c1; q++) {
+        uint32_t v = pbits(A[q]);
+        cl += (v <= P);
+        cr += (v >= P);
+    }
+    int totL, totR;
+    const int baseL = tie_excl_scan(cl, red, &totL);
+    const int baseR = tie_excl_scan(cr, red, &totR);
+    int aL = baseL;
+    int rAfter = totR - baseR;  // #R in [c0, hi]
+    int nswap = 0;
+    for (int q = c0; q < c1; q++) {
+        uint32_t v = pbits(A[q]);
+        const bool isL = v <= P, isR = v >= P;
+        if (isL) {
+            aL++;
+            posL[aL - 1] = q;
+            if (rAfter >= aL) nswap++;
+        }
+        if (isR) {
+            posR[rAfter - 1] = q;
+            rAfter--;
+        }
+    }
+    const int T = tie_sum(nswap, red);
+    __syncthreads();  // posL / posR complete
+    for (int t = tid; t < T; t += kTieThreads) {
+        const int x = posL[t], y = posR[t];
+        if (x != y) {
+            unsigned long long a = A[x];
+            A[x] = A[y];
+            A[y] = a;
+        }
+    }
+    if (tid == 0) {
+        int i, j;
+        if (T == 0) {
+            i = posL[0];
+            j = posR[0];
+        } else {
+            const int x = posL[T - 1], y = posR[T - 1];
+            if (x == y) { i = x + 1; j = x - 1; }
+            else if (y == x + 1) { i = y; j = x; }
+            else {
+                const int nl = (T < totL) ? posL[T] : 0x7fffffff;
+                const int nr = (T < totR) ? posR[T] : -0x7fffffff;
+                i = min(nl, y);
+                j = max(nr, x);
+            }
+        }
+        sh[0] = i;
+        sh[1] = j;
+    }
+    __syncthreads();
+    *oi = sh[0];
+    *oj = sh[1];
+    __syncthreads();
+}
+
+__device__ void tie_sort_desc(unsigned long long* a, int n) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < n / 2; i += kTieThreads) {
+                int lo = 2 * stride * (i / stride) + (i % stride);
+                int hi = lo + stride;
+                bool desc = ((lo & size) == 0);
+                unsigned long long x = a[lo], y = a[hi];
+                if ((x < y) == desc) { a[lo] = y; a[hi] = x; }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTieThreads)
+ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __restrict__ ov_n,
+            const int* __restrict__ ov_idx, const float* __restrict__ ov_val, int ov_stride,
+            const int* __restrict__ slow_list, const int* __restrict__ slow_count,
+            RowResult* __restrict__ res, unsigned long long* __restrict__ scratch,
+            int* __restrict__ pos_scratch, int* __restrict__ cand_index_out,
+            float* __restrict__ cand_prob_out, int cand_cap) {
+    __shared__ int red[32];
+    __shared__ int sh[4];
+    __shared__ unsigned long long sk[kCandCap];
+    extern __shared__ unsigned char dyn[];
+    int* ovi = reinterpret_cast<int*>(dyn);
+    float* ovv = reinterpret_cast<float*>(ovi + (ov_stride > 0 ? ov_stride : 1));
+
+    const int tid = threadIdx.x;
+    unsigned long long* A = scratch + (size_t)blockIdx.x * V;
+    int* posL = pos_scratch + (size_t)blockIdx.x * 2 * V;
+    int* posR = posL + V;
+    const int nslow = *slow_count;
+    const int k = prm.top_k;
+
+    for (int li = blockIdx.x; li < nslow; li += gridDim.x) {
+        const int row = slow_list[li];
+        const RowResult rr = res[row];
+        const T* L = logits + (size_t)row * V;
+        const int nov = ov_n ? ov_n[row] : 0;
+        for (int i = tid; i < nov; i += kTieThreads) {
+            ovi[i] = ov_idx[(size_t)row * ov_stride + i];
+            ovv[i] = ov_val[(size_t)row * ov_stride + i];
+        }
+        __syncthreads();
+        // probindex as sample() leaves it before selection (sampler.h:195-207)
+        for (int i = tid; i < V; i += kTieThreads) {
+            float l = Elem<T>::widen(L[i]);
+            if (nov) {
+                int lo = 0, hi = nov;
+                while (lo < hi) { int m = (lo + hi) >> 1; if (ovi[m] < i) lo = m + 1; else hi = m; }
+                if (lo < nov && ovi[lo] == i) l = ovv[lo];
+            }
+            const float t = __fmul_rn(l, rr.inv_temp);
+            const float e = expf(__fsub_rn(t, rr.max_logit));
+            const float p = __fmul_rn(e, rr.sum_inv);
+            A[i] = ((unsigned long long)__float_as_uint(p) << 32) | (unsigned)i;
+        }
+        __syncthreads();
+        // quick_select(probindex, V, k - 1)  (sampler.h:76-94)
+        int lo = 0, hi = V - 1;
+        const int kk = k - 1;
+        long long rounds = 0;
+        const long long max_rounds = 4ll * V + 64;  // the serial loop needs far fewer
+        while (lo < hi && rounds++ < max_rounds) {
+            const uint32_t P = pbits(A[kk]);
+            __syncthreads();
+            int i, j;
+            partition_round(A, lo, hi, P, posL, posR, red, sh, &i, &j);
+            if (j < kk) lo = i;
+            if (i > kk) hi = j;
+        }
+        // stable qsort of the first k by probability, descending (sampler.h:214)
+        int npow = 1;
+        while (npow < k) npow <<= 1;
+        for (int i = tid; i < npow; i += kTieThreads) {
+            sk[i] = (i < k) ? (((unsigned long long)pbits(A[i]) << 32) |
+                               (unsigned long long)(0xFFFFFFFFu - (uint32_t)i))
+                            : 0ull;
+        }
+        __syncthreads();
+        tie_sort_desc(sk, npow);
+        // min-p, top-p, renormalise, draw on the exact order (thread 0)
+        if (tid == 0) {
+            auto P = [&](int i) { return __uint_as_float((uint32_t)(sk[i] >> 32)); };
+            auto I = [&](int i) {
+                const int pos = (int)(0xFFFFFFFFu - (uint32_t)(sk[i] & 0xFFFFFFFFull));
+                return (int)(uint32_t)(A[pos] & 0xFFFFFFFFull);
+            };
+            int n = k;
+            if (prm.minp > 0.0f) {
+                float pmax = P(0);
+                for (int i = 1; i < n; i++) if (P(i) > pmax) pmax = P(i);
+                const float thrp = __fmul_rn(prm.minp, pmax);
+                int kept = 0;
+                while (kept < n && P(kept) >= thrp) kept++;
+                n = kept > 0 ? kept : 1;
+            }
+            const int n_minp = n;
+            if (prm.topp < 1.0f && prm.topp > 0.0f) {
+                float cum = 0.f;
+                int cut = 0;
+                for (int i = 0; i < n; i++) {
+                    cum = __fadd_rn(cum, P(i));
+                    if (cum >= prm.topp) { cut = i + 1; break; }
+                }
+                if (cut > 0) n = cut;
+            }
+            float s2 = 0.f;
+            for (int i = 0; i < n; i++) s2 = __fadd_rn(s2, P(i));
+            const float inv2 = __fdiv_rn(1.0f, s2);
+            float cum = 0.f;
+            int pos = n - 1;
+            for (int i = 0; i < n; i++) {
+                cum = __fadd_rn(cum, __fmul_rn(P(i), inv2));
+                if (rr.r < cum) { pos = i; break; }
+            }
+            RowResult o = rr;
+            o.token = I(pos);
+            o.n_topk = k;
+            o.n_minp = n_minp;
+            o.n_final = n;
+            o.renorm_sum = s2;
+            o.draw_pos = pos;
+            o.exact_ties = 1;
+            o.status = 0;
+            res[row] = o;
+            if (cand_index_out) {
+                const int lim = min(k, cand_cap);
+                for (int i = 0; i < lim; i++) {
+                    cand_index_out[(size_t)row * cand_cap + i] = I(i);
+                    cand_prob_out[(size_t)row * cand_cap + i] = i < n ? __fmul_rn(P(i), inv2) : P(i);
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+template <typename T>
+cudaError_t launch_ties_kernel(const T* logits, int V, TieParams prm, const int* ov_n,
+                               const int* ov_idx, const float* ov_val, int ov_stride,
+                               const int* slow_list, const int* slow_count, RowResult* res,
+                               unsigned long long* scratch, int* pos_scratch, int nctas,
+                               int* cand_index, float* cand_prob, int cand_cap,
+                               cudaStream_t stream) {
+    const size_t smem = 8 * (size_t)(ov_stride > 0 ? ov_stride : 1) + 16;
+    ties_kernel<T><<<nctas, kTieThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val,
+                                                         ov_stride, slow_list, slow_count, res,
+                                                         scratch, pos_scratch, cand_index,
+                                                         cand_prob, cand_cap);
+    return cudaGetLastError();
+}
+
+template cudaError_t launch_ties_kernel<float>(const float*, int, TieParams, const int*, const int*,
+                                               const float*, int, const int*, const int*,
+                                               RowResult*, unsigned long long*, int*, int, int*,
+                                               float*, int, cudaStream_t);
+template cudaError_t launch_ties_kernel<__nv_bfloat16>(const __nv_bfloat16*, int, TieParams,
+                                                       const int*, const int*, const float*, int,
+                                                       const int*, const int*, RowResult*,
+                                                       unsigned long long*, int*, int, int*,
+                                                       float*, int, cudaStream_t);
+
+// ------------------------------------------------------------- epilogue
+// Copies tokens out and, for the stateful API, records each row's token in
+// its history exactly as sampler.h:257-267 does.
+__global__ void emit_kernel(int B, int V, int W, const RowResult* __restrict__ res,
+                            int* __restrict__ tokens, qs_row_debug_dev* dbg, int* ring,
+                            int* hcount, int* hpos, float* token_counts) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= B) return;
+    const RowResult rr = res[r];
+    tokens[r] = rr.token;
+    if (dbg) {
+        qs_row_debug_dev d;
+        d.token = rr.token; d.greedy = rr.greedy; d.n_topk = rr.n_topk; d.n_minp = rr.n_minp;
+        d.n_final = rr.n_final; d.draw_pos = rr.draw_pos; d.exact_ties = rr.exact_ties;
+        d.sum_fallback = rr.sum_fallback; d.max_logit = rr.max_logit; d.sum = rr.sum; d.r = rr.r;
+        d.renorm_sum = rr.renorm_sum;
+        dbg[r] = d;
+    }
+    if (ring && W > 0 && rr.token >= 0 && rr.token < V) {
+        token_counts[(size_t)r * V + rr.token] += 1.0f;
+        int p = hpos[r];
+        ring[(size_t)r * W + p] = rr.token;
+        hpos[r] = (p + 1) % W;
+        if (hcount[r] < W) hcount[r] = hcount[r] + 1;
+    }
+}
+
+cudaError_t launch_emit(int B, int V, int W, const RowResult* res, int* tokens,
+                        qs_row_debug_dev* dbg, int* ring, int* hcount, int* hpos,
+                        float* token_counts, cudaStream_t stream) {
+    emit_kernel<<<(B + 127) / 128, 128, 0, stream>>>(B, V, W, res, tokens, dbg, ring, hcount, hpos,
+                                                      token_counts);
+    return cudaGetLastError();
+}
+
+// Full normalised softmax for diagnostics (sampler.h:204-207).
+template <typename T>
+__global__ void probs_kernel(const T* __restrict__ logits, int V, const int* __restrict__ ov_n,
+                             const int* __restrict__ ov_idx, const float* __restrict__ ov_val,
+                             int ov_stride, const RowResult* __restrict__ res,
+                             float* __restrict__ probs) {
+    const int row = blockIdx.y;
+    const RowResult rr = res[row];
+    const T* L = logits + (size_t)row * V;
+    const int nov = ov_n ? ov_n[row] : 0;
+    const int* oi = ov_idx ? ov_idx + (size_t)row * ov_stride : nullptr;
+    const float* ovp = ov_val ? ov_val + (size_t)row * ov_stride : nullptr;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+        float l = Elem<T>::widen(L[i]);
+        if (nov) {
+            int lo = 0, hi = nov;
+            while (lo < hi) { int m = (lo + hi) >> 1; if (oi[m] < i) lo = m + 1; else hi = m; }
+            if (lo < nov && oi[lo] == i) l = ovp[lo];
+        }
+        float p = 0.0f;
+        if (!rr.greedy) {
+            const float t = __fmul_rn(l, rr.inv_temp);
+            p = __fmul_rn(expf(__fsub_rn(t, rr.max_logit)), rr.sum_inv);
+        }
+        probs[(size_t)row * V + i] = p;
+    }
+}
+
+template <typename T>
+cudaError_t launch_probs(const T* logits, int B, int V, const int* ov_n, const int* ov_idx,
+                         const float* ov_val, int ov_stride, const RowResult* res, float* probs,
+                         cudaStream_t stream) {
+    dim3 grid(64, B);
+    probs_kernel<T><<<grid, 256, 0, stream>>>(logits, V, ov_n, ov_idx, ov_val, ov_stride, res, probs);
+    return cudaGetLastError();
+}
+
+template cudaError_t launch_probs<float>(const float*, int, int, const int*, const int*, const float*,
+                                         int, const RowResult*, float*, cudaStream_t);
+template cudaError_t launch_probs<__nv_bfloat16>(const __nv_bfloat16*, int, int, const int*,
+                                                 const int*, const float*, int, const RowResult*,
+                                                 float*, cudaStream_t);
+
+}  // namespace qs
