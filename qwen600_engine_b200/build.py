@@ -20,7 +20,8 @@ LIB = os.path.join(HERE, "libqwen600_sampler.so")
 SOURCES = ["qs_penalty.cu", "qs_row.cu", "qs_ties.cu", "qs_api.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "--fmad=false", "-std=c++17", "-Xcompiler", "-fPIC",
-         "-Xcompiler", "-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-I", CSRC]
+         "-Xcompiler", "-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-I", CSRC,
+         "-I", OUT_DIR]
 
 
 def nvcc() -> str:
@@ -37,9 +38,43 @@ def _stale(target: str, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def exp_table(verbose: bool = False) -> str:
+    """Generates _build/qs_exp_table.inc: the inputs where the host libm's
+    expf (what the reference sampler calls) rounds differently from
+    qs_exp_rn.  Takes about a minute; redone only when its sources change."""
+    os.makedirs(OUT_DIR, exist_ok=True)
+    inc = os.path.join(OUT_DIR, "qs_exp_table.inc")
+    gen_src = os.path.join(CSRC, "qs_exp_table.c")
+    deps = [gen_src, os.path.join(CSRC, "qs_exp.h")]
+    if not _stale(inc, deps):
+        return inc
+    exe = os.path.join(OUT_DIR, "qs_exp_table")
+    cc = shutil.which("gcc") or "cc"
+    flags = ["-O2", "-ffp-contract=off"]
+    try:
+        if " fma " in open("/proc/cpuinfo").read():
+            flags.append("-mfma")  # hardware fma: same IEEE result, faster scan
+    except OSError:
+        pass
+    r = subprocess.run([cc] + flags + ["-I", CSRC, "-o", exe, gen_src, "-lm"],
+                       capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"compiling qs_exp_table.c failed:\n{r.stderr}")
+    tmp = inc + ".tmp"
+    r = subprocess.run([exe, tmp], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"qs_exp_table failed:\n{r.stderr}")
+    os.replace(tmp, inc)
+    if verbose:
+        print(r.stdout.strip())
+    return inc
+
+
 def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) -> str:
     os.makedirs(OUT_DIR, exist_ok=True)
-    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")]
+    table = exp_table(verbose)
+    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    headers.append(table)
     headers.append(os.path.join(ROOT, "include", "qwen600_sampler.h"))
     objs = []
     for src in SOURCES:

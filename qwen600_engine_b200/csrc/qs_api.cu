@@ -28,16 +28,19 @@ size_t row_kernel_smem(int V, int dtype_bytes, int ov_stride);
 template <typename T>
 cudaError_t launch_row_kernel(const T*, int, int, RowParams, const int*, const int*, const float*,
                               int, unsigned long long*, RowResult*, int*, int*, int*, float*, int,
-                              cudaStream_t);
+                              ExpFix, cudaStream_t);
 template <typename T>
 cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
                                const int*, const int*, RowResult*, unsigned long long*, int*, int,
-                               int*, float*, int, cudaStream_t);
+                               int*, float*, int, ExpFix, cudaStream_t);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, cudaStream_t);
 template <typename T>
 cudaError_t launch_probs(const T*, int, int, const int*, const int*, const float*, int,
-                         const RowResult*, float*, cudaStream_t);
+                         const RowResult*, float*, ExpFix, cudaStream_t);
+
+// host copy of the libm expf correction table (generated at build time)
+#include "qs_exp_table.inc"
 
 }  // namespace qs
 
@@ -90,6 +93,10 @@ struct qs_sampler {
     // host-entry staging
     float* d_in = nullptr;
     int* d_tok = nullptr;
+    // expf correction table on the device
+    uint32_t* exp_off = nullptr;
+    uint32_t* exp_ent = nullptr;
+    ExpFix fix() const { return ExpFix{exp_off, exp_ent, (uint32_t)QS_EXP_NB}; }
 };
 
 static void release(qs_sampler* s) {
@@ -99,7 +106,7 @@ static void release(qs_sampler* s) {
     cudaSetDevice(s->device);
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts,
-                    s->rng, s->d_in, s->d_tok};
+                    s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (s->stream) cudaStreamDestroy(s->stream);
@@ -180,6 +187,8 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     ALLOC(s->rng, sizeof(unsigned long long) * B);
     ALLOC(s->d_in, sizeof(float) * B * V);
     ALLOC(s->d_tok, sizeof(int) * B);
+    ALLOC(s->exp_off, sizeof(qs_exp_fix_off));
+    ALLOC(s->exp_ent, sizeof(qs_exp_fix_ent));
     if (W > 0) {
         ALLOC(s->ring, sizeof(int) * B * W);
         ALLOC(s->hcount, sizeof(int) * B);
@@ -195,6 +204,10 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     std::vector<unsigned long long> st(B);
     for (size_t r = 0; r < B; r++) st[r] = seed + r;
     e = cudaMemcpy(s->rng, st.data(), sizeof(unsigned long long) * B, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(s->exp_off, qs_exp_fix_off, sizeof(qs_exp_fix_off), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(s->exp_ent, qs_exp_fix_ent, sizeof(qs_exp_fix_ent), cudaMemcpyHostToDevice);
     if (e == cudaSuccess && W > 0) {
         e = cudaMemset(s->hcount, 0, sizeof(int) * B);
         if (e == cudaSuccess) e = cudaMemset(s->hpos, 0, sizeof(int) * B);
@@ -338,12 +351,12 @@ static int run(qs_sampler* s, const Call& c) {
     if (c.dtype == QS_F32) {
         CK(launch_row_kernel<float>((const float*)c.logits, B, V, rp, ovn, s->ov_idx, s->ov_val,
                                     s->ov_stride, c.rng, s->res, s->slow_list, s->slow_count,
-                                    c.cand_index, c.cand_prob, c.cand_cap, c.stream));
+                                    c.cand_index, c.cand_prob, c.cand_cap, s->fix(), c.stream));
     } else {
         CK(launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, ovn,
                                             s->ov_idx, s->ov_val, s->ov_stride, c.rng, s->res,
                                             s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
-                                            c.cand_cap, c.stream));
+                                            c.cand_cap, s->fix(), c.stream));
     }
     if (!greedy && topk && !(c.flags & QS_FLAG_INDEX_TIES)) {
         TieParams tp{p.temperature, p.topp, p.minp, p.top_k};
@@ -352,21 +365,21 @@ static int run(qs_sampler* s, const Call& c) {
             CK(launch_ties_kernel<float>((const float*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val,
                                          s->ov_stride, s->slow_list, s->slow_count, s->res,
                                          s->tie_scratch, s->tie_pos, nct, c.cand_index, c.cand_prob,
-                                         c.cand_cap, c.stream));
+                                         c.cand_cap, s->fix(), c.stream));
         } else {
             CK(launch_ties_kernel<__nv_bfloat16>(
                 (const __nv_bfloat16*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val, s->ov_stride,
                 s->slow_list, s->slow_count, s->res, s->tie_scratch, s->tie_pos, nct, c.cand_index,
-                c.cand_prob, c.cand_cap, c.stream));
+                c.cand_prob, c.cand_cap, s->fix(), c.stream));
         }
     }
     if (c.probs) {
         if (c.dtype == QS_F32)
             CK(launch_probs<float>((const float*)c.logits, B, V, ovn, s->ov_idx, s->ov_val,
-                                   s->ov_stride, s->res, c.probs, c.stream));
+                                   s->ov_stride, s->res, c.probs, s->fix(), c.stream));
         else
             CK(launch_probs<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, ovn, s->ov_idx,
-                                           s->ov_val, s->ov_stride, s->res, c.probs, c.stream));
+                                           s->ov_val, s->ov_stride, s->res, c.probs, s->fix(), c.stream));
     }
     CK(launch_emit(B, V, s->window, s->res, c.tokens, c.dbg, c.ring, c.hcount, c.hpos,
                    c.token_counts, c.stream));

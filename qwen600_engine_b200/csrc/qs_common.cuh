@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "qs_exp.cuh"
 #include "qwen600_sampler.h"
 
 namespace qs {

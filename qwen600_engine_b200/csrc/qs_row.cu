@@ -182,7 +182,8 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
            const float* __restrict__ ov_val, int ov_stride,
            unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
            int* __restrict__ slow_list, int* __restrict__ slow_count,
-           int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap) {
+           int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
+           ExpFix fx) {
     constexpr int EPL = Elem<T>::kPerLane;
     constexpr int SEG = 32 * EPL;
     constexpr int U = 4;  // segments in flight per warp in the streaming pass
@@ -377,7 +378,8 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
     // element helper: exact reference exponent of a penalised logit
     auto t_of = [&](float l) { return __fmul_rn(l, inv); };
 
-    // ---- C1: approximate sums of hot segments
+    // ---- C1: approximate sums of hot segments (only used to predict binades,
+    //      so CUDA's expf is good enough here; exact values come from ref_expf)
     for (int h = warp; h < nhot; h += kWarps) {
         float v[EPL];
         load_seg(hot[h], v);
@@ -444,7 +446,7 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
 #pragma unroll
         for (int e = 0; e < EPL; e++) {
             float t = t_of(v[e]);
-            float ev = (t >= thr) ? expf(__fsub_rn(t, M)) : 0.0f;
+            float ev = (t >= thr) ? ref_expf(__fsub_rn(t, M), fx) : 0.0f;
             f = tf_compose(f, tf_element(ev, E));
         }
 #pragma unroll
@@ -484,7 +486,7 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
 #pragma unroll
                 for (int e = 0; e < EPL; e++) {
                     float t = t_of(v[e]);
-                    ev[e] = (t >= thr) ? expf(__fsub_rn(t, M)) : 0.0f;
+                    ev[e] = (t >= thr) ? ref_expf(__fsub_rn(t, M), fx) : 0.0f;
                 }
                 for (int src = 0; src < 32; src++) {
 #pragma unroll
@@ -539,7 +541,7 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
         while (npow < c) npow <<= 1;
         for (int i = tid; i < npow; i += kThreads) {
             if (i < c) {
-                float e = expf(__fsub_rn(ct[i], M));
+                float e = ref_expf(__fsub_rn(ct[i], M), fx);
                 float pr = __fmul_rn(e, sum_inv);
                 ck[i] = ((unsigned long long)__float_as_uint(pr) << 32) |
                         (unsigned long long)(0xFFFFFFFFu - (uint32_t)ci[i]);
@@ -691,24 +693,24 @@ cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, cons
                               const int* ov_idx, const float* ov_val, int ov_stride,
                               unsigned long long* rng, RowResult* res, int* slow_list,
                               int* slow_count, int* cand_index, float* cand_prob, int cand_cap,
-                              cudaStream_t stream) {
+                              ExpFix fx, cudaStream_t stream) {
     const size_t smem = row_kernel_smem(V, (int)sizeof(T), ov_stride);
     cudaError_t err = cudaFuncSetAttribute(row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err != cudaSuccess) return err;
     row_kernel<T><<<B, kThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val, ov_stride,
                                                  rng, res, slow_list, slow_count, cand_index,
-                                                 cand_prob, cand_cap);
+                                                 cand_prob, cand_cap, fx);
     return cudaGetLastError();
 }
 
 template cudaError_t launch_row_kernel<float>(const float*, int, int, RowParams, const int*,
                                               const int*, const float*, int, unsigned long long*,
-                                              RowResult*, int*, int*, int*, float*, int,
+                                              RowResult*, int*, int*, int*, float*, int, ExpFix,
                                               cudaStream_t);
 template cudaError_t launch_row_kernel<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams,
                                                       const int*, const int*, const float*, int,
                                                       unsigned long long*, RowResult*, int*, int*,
-                                                      int*, float*, int, cudaStream_t);
+                                                      int*, float*, int, ExpFix, cudaStream_t);
 
 }  // namespace qs

@@ -158,7 +158,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             const int* __restrict__ slow_list, const int* __restrict__ slow_count,
             RowResult* __restrict__ res, unsigned long long* __restrict__ scratch,
             int* __restrict__ pos_scratch, int* __restrict__ cand_index_out,
-            float* __restrict__ cand_prob_out, int cand_cap) {
+            float* __restrict__ cand_prob_out, int cand_cap, ExpFix fx) {
     __shared__ int red[32];
     __shared__ int sh[4];
     __shared__ unsigned long long sk[kCandCap];
@@ -192,7 +192,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                 if (lo < nov && ovi[lo] == i) l = ovv[lo];
             }
             const float t = __fmul_rn(l, rr.inv_temp);
-            const float e = expf(__fsub_rn(t, rr.max_logit));
+            const float e = ref_expf(__fsub_rn(t, rr.max_logit), fx);
             const float p = __fmul_rn(e, rr.sum_inv);
             A[i] = ((unsigned long long)__float_as_uint(p) << 32) | (unsigned)i;
         }
@@ -282,25 +282,25 @@ cudaError_t launch_ties_kernel(const T* logits, int V, TieParams prm, const int*
                                const int* ov_idx, const float* ov_val, int ov_stride,
                                const int* slow_list, const int* slow_count, RowResult* res,
                                unsigned long long* scratch, int* pos_scratch, int nctas,
-                               int* cand_index, float* cand_prob, int cand_cap,
+                               int* cand_index, float* cand_prob, int cand_cap, ExpFix fx,
                                cudaStream_t stream) {
     const size_t smem = 8 * (size_t)(ov_stride > 0 ? ov_stride : 1) + 16;
     ties_kernel<T><<<nctas, kTieThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val,
                                                          ov_stride, slow_list, slow_count, res,
                                                          scratch, pos_scratch, cand_index,
-                                                         cand_prob, cand_cap);
+                                                         cand_prob, cand_cap, fx);
     return cudaGetLastError();
 }
 
 template cudaError_t launch_ties_kernel<float>(const float*, int, TieParams, const int*, const int*,
                                                const float*, int, const int*, const int*,
                                                RowResult*, unsigned long long*, int*, int, int*,
-                                               float*, int, cudaStream_t);
+                                               float*, int, ExpFix, cudaStream_t);
 template cudaError_t launch_ties_kernel<__nv_bfloat16>(const __nv_bfloat16*, int, TieParams,
                                                        const int*, const int*, const float*, int,
                                                        const int*, const int*, RowResult*,
                                                        unsigned long long*, int*, int, int*,
-                                                       float*, int, cudaStream_t);
+                                                       float*, int, ExpFix, cudaStream_t);
 
 // ------------------------------------------------------------- epilogue
 // Copies tokens out and, for the stateful API, records each row's token in
@@ -342,7 +342,7 @@ template <typename T>
 __global__ void probs_kernel(const T* __restrict__ logits, int V, const int* __restrict__ ov_n,
                              const int* __restrict__ ov_idx, const float* __restrict__ ov_val,
                              int ov_stride, const RowResult* __restrict__ res,
-                             float* __restrict__ probs) {
+                             float* __restrict__ probs, ExpFix fx) {
     const int row = blockIdx.y;
     const RowResult rr = res[row];
     const T* L = logits + (size_t)row * V;
@@ -359,7 +359,7 @@ __global__ void probs_kernel(const T* __restrict__ logits, int V, const int* __r
         float p = 0.0f;
         if (!rr.greedy) {
             const float t = __fmul_rn(l, rr.inv_temp);
-            p = __fmul_rn(expf(__fsub_rn(t, rr.max_logit)), rr.sum_inv);
+            p = __fmul_rn(ref_expf(__fsub_rn(t, rr.max_logit), fx), rr.sum_inv);
         }
         probs[(size_t)row * V + i] = p;
     }
@@ -368,16 +368,16 @@ __global__ void probs_kernel(const T* __restrict__ logits, int V, const int* __r
 template <typename T>
 cudaError_t launch_probs(const T* logits, int B, int V, const int* ov_n, const int* ov_idx,
                          const float* ov_val, int ov_stride, const RowResult* res, float* probs,
-                         cudaStream_t stream) {
+                         ExpFix fx, cudaStream_t stream) {
     dim3 grid(64, B);
-    probs_kernel<T><<<grid, 256, 0, stream>>>(logits, V, ov_n, ov_idx, ov_val, ov_stride, res, probs);
+    probs_kernel<T><<<grid, 256, 0, stream>>>(logits, V, ov_n, ov_idx, ov_val, ov_stride, res, probs, fx);
     return cudaGetLastError();
 }
 
 template cudaError_t launch_probs<float>(const float*, int, int, const int*, const int*, const float*,
-                                         int, const RowResult*, float*, cudaStream_t);
+                                         int, const RowResult*, float*, ExpFix, cudaStream_t);
 template cudaError_t launch_probs<__nv_bfloat16>(const __nv_bfloat16*, int, int, const int*,
                                                  const int*, const float*, int, const RowResult*,
-                                                 float*, cudaStream_t);
+                                                 float*, ExpFix, cudaStream_t);
 
 }  // namespace qs
