@@ -1,0 +1,410 @@
+#!/usr/bin/env python
+"""Benchmark: sampled rows/s of the B200 token sampler.
+
+Workload (one step = one batch of rows through the whole sampler):
+  top-k sampling over bf16 logit rows of the Qwen3-0.6B vocabulary
+  (V = 151936), 1024 rows per GPU drawn 4*Gumbel(0,1) plus a per-row offset
+  U[-8, 8]; a 64-token window per row drawn uniformly over V; temperature 0.7,
+  top-k 50, top-p 0.95, min-p 0.1, repetition penalty 1.15.  Synthetic data
+  (the reference publishes no sampler dataset); rows are independent, so
+  with N GPUs each rank samples its own 1024 rows (weak scaling) and the
+  tokens are gathered to rank 0 on a side stream.
+
+Reported (one JSON line on rank 0):
+  value       rows/s of the whole job, logits already in HBM, device time
+              (CUDA events on the launching stream, max over ranks); two
+              distinct logit buffers (2 x 311 MB, above the 126 MB L2) are
+              used in turn so that every step streams its rows from HBM.
+  e2e         rows/s through the C ABI with host buffers: each step copies
+              its logits, window and RNG states from pinned host memory and
+              reads the tokens back.
+  roofline    the fused row kernel's algorithmic bytes per launch (the bf16
+              logits it must read, 303,872 B per row) over its average
+              launch time, against MEASURED_PEAKS.json's HBM copy bandwidth.
+  cpu_baseline  the reference's own sampler.h (oracle/_ref, compiled from the
+              reference tree) on this host's cores, on a bounded sample.
+
+`--impl reference` times that CPU sampler as the job itself (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+V = 151936
+WINDOW = 64
+PARAMS = dict(temperature=0.7, topp=0.95, minp=0.1, top_k=50, repetition_penalty=1.15,
+              frequency_penalty=0.0, presence_penalty=0.0)
+METRIC = "sampled rows/sec @V=151936 (B=1/64/1024), % of HBM roofline, 1/2/4/8 GPU"
+WORKLOAD = ("top-k sampling, bf16 logits 4*Gumbel+U[-8,8] per row, V=151936, 1024 rows/GPU, "
+            "64-token uniform window, T=0.7 k=50 p=0.95 min-p=0.1 rep=1.15")
+ROW_BYTES = V * 2            # logits the row kernel must read per row (bf16)
+STEP_ROW_BYTES = V * 2 + WINDOW * 4   # plus the window ids (penalty kernel)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed
+    region (read only)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference_sample(target_s: float = 15.0, seed: int = 4):
+    """Times the reference's own sampler.h (oracle/_ref) on this host's cores
+    over a bounded sample of the workload; falls back to the oracle port."""
+    import numpy as np
+
+    from qwen600_engine_b200 import workloads as W
+    threads = os.cpu_count() or 1
+    kind = "reference"
+    try:
+        from oracle.oracle import RefSampler
+        ref = RefSampler()
+        run = lambda wl, x: ref.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
+                                            wl.hist_count, wl.hist_pos, wl.rng, n_threads=threads)
+    except Exception:
+        from oracle.oracle import Oracle
+        kind, threads = "port", 1
+        o = Oracle()
+        run = lambda wl, x: o.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
+                                          wl.hist_count, wl.rng)
+    # the reference samples fp32 rows on the host (bf16 widened on the GPU
+    # before its copy-out), so widening happens outside the timed calls
+    probe = W.topk_bf16(B=min(64, 8 * threads), seed=seed)
+    px = probe.logits_f32()
+    t0 = time.perf_counter()
+    run(probe, px)
+    dt = time.perf_counter() - t0
+    per_row = dt / probe.batch
+    rows = int(max(probe.batch, min(2048, target_s / max(per_row, 1e-6))))
+    wl = W.topk_bf16(B=rows, seed=seed + 100)
+    wx = wl.logits_f32()
+    t0 = time.perf_counter()
+    run(wl, wx)
+    dt = time.perf_counter() - t0
+    return {"value": rows / dt, "unit": "rows/s", "cores": threads, "kind": kind,
+            "sample": f"{rows} rows of the benchmark workload (seed {seed + 100}), "
+                      f"{dt:.1f} s on {threads} host threads",
+            "seconds": dt, "rows": rows}
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from qwen600_engine_b200 import workloads as W
+    threads = os.cpu_count() or 1
+    try:
+        from oracle.oracle import RefSampler
+        ref = RefSampler()
+        kind = "reference"
+        run = lambda wl, x: ref.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
+                                            wl.hist_count, wl.hist_pos, wl.rng, n_threads=threads)
+    except Exception:
+        from oracle.oracle import Oracle
+        o = Oracle()
+        kind, threads = "port", 1
+        run = lambda wl, x: o.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
+                                          wl.hist_count, wl.rng)
+    rows = max(threads * 2, 32)
+    batches = [W.topk_bf16(B=rows, seed=4 + 1000 * i) for i in range(2)]
+    xs = [b.logits_f32() for b in batches]   # widened outside the timing (see cpu_reference_sample)
+    for i in range(args.warmup):
+        run(batches[i % 2], xs[i % 2])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        run(batches[i % 2], xs[i % 2])
+    dt = time.perf_counter() - t0
+    v = rows * args.steps / dt
+    line = {"metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": rows, "vocab": V,
+                       "rows_per_step": rows, "note": "each step a bounded CPU sample"},
+            "cpu_baseline": {"value": v, "unit": "rows/s", "cores": threads, "kind": kind,
+                             "sample": f"{rows} rows per step x {args.steps} steps"},
+            "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def make_inputs(torch, B, seed, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    u = torch.rand((B, V), generator=g, device=device, dtype=torch.float32).clamp_(1e-12, 1 - 1e-7)
+    off = (torch.rand((B, 1), generator=g, device=device) * 16.0 - 8.0)
+    logits = (4.0 * (-torch.log(-torch.log(u))) + off).to(torch.bfloat16)
+    del u
+    hist = torch.randint(0, V, (B, WINDOW), generator=g, device=device, dtype=torch.int32)
+    counts = torch.ones((B, WINDOW), device=device, dtype=torch.float32)
+    count = torch.full((B,), WINDOW, device=device, dtype=torch.int32)
+    rng = (torch.arange(B, device=device, dtype=torch.int64) + seed * 1000003 + 1)
+    return logits, hist, counts, count, rng
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1024, help="rows per GPU")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from qwen600_engine_b200.sampler import Sampler
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    B = args.batch
+
+    bufs = [make_inputs(torch, B, 4 + 7919 * rank + 104729 * i, dev) for i in range(2)]
+    hist, counts, count = bufs[0][1], bufs[0][2], bufs[0][3]
+    rng = bufs[0][4].clone()
+    toks = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
+    glist = [[torch.empty(B, dtype=torch.int32, device=dev) for _ in range(world)]
+             for _ in range(2)] if (world > 1 and rank == 0) else [None, None]
+    s = Sampler(PARAMS["temperature"], PARAMS["topp"], PARAMS["minp"], PARAMS["top_k"],
+                PARAMS["repetition_penalty"], PARAMS["frequency_penalty"],
+                PARAMS["presence_penalty"], WINDOW, 1, max_batch=B, vocab=V, device=local)
+    main_stream = torch.cuda.current_stream()
+    gstream = torch.cuda.Stream() if world > 1 else None
+    gdone = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def step(i):
+        j = i % 2
+        if world > 1 and i >= 2:
+            main_stream.wait_event(gdone[j])
+        s.sample_rows(bufs[j][0], hist, counts, count, rng, out=toks[j])
+        if world > 1:
+            ev = torch.cuda.Event()
+            ev.record(main_stream)
+            with torch.cuda.stream(gstream):
+                gstream.wait_event(ev)
+                dist.gather(toks[j], gather_list=glist[j], dst=0)
+                gdone[j].record(gstream)
+
+    def sync_all():
+        if gstream is not None:
+            main_stream.wait_stream(gstream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        step(i)
+    sync_all()
+
+    # ---- timed region (device time, launching stream)
+    prof0 = s.profile_read()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record(main_stream)
+        for i in range(args.steps):
+            step(i)
+        if gstream is not None:
+            main_stream.wait_stream(gstream)
+        t1.record(main_stream)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    prof1 = s.profile_read()
+    launches = int(prof1["launches"] - prof0["launches"])
+    sync_all()
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * B / (ms_step / 1e3)
+
+    # ---- per-kernel timing of the same steps (separate pass, events around each kernel)
+    s.profile(True)
+    s.profile_reset()
+    for i in range(args.steps):
+        step(i)
+    sync_all()
+    pr = s.profile_read()
+    s.profile(False)
+    row_ms = pr["row_ms"] / max(pr["row_launches"], 1)
+    hbm, peak_kind = peaks()
+    achieved = B * ROW_BYTES / (row_ms / 1e3) / 1e9
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "row_kernel_topk_bf16.txt")
+    if os.path.exists(tfile):
+        for ln in open(tfile):
+            if ln.startswith("dram_bytes_per_launch_B1024:"):
+                try:
+                    traffic = float(ln.split(":", 1)[1].split()[0])
+                except ValueError:
+                    pass
+
+    # ---- end to end through the C ABI with host buffers
+    e2e = None
+    if args.e2e_steps > 0:
+        h_logits = [bufs[i][0].cpu().pin_memory() for i in range(2)]
+        h_hist, h_counts, h_count = hist.cpu().pin_memory(), counts.cpu().pin_memory(), count.cpu().pin_memory()
+        h_rng = rng.cpu().pin_memory()
+        h_tok = torch.empty(B, dtype=torch.int32).pin_memory()
+        d_logits = torch.empty_like(bufs[0][0])
+        d_hist, d_counts, d_count = torch.empty_like(hist), torch.empty_like(counts), torch.empty_like(count)
+        d_rng = torch.empty_like(rng)
+        d_tok = torch.empty(B, dtype=torch.int32, device=dev)
+
+        def e2e_step(i):
+            d_logits.copy_(h_logits[i % 2], non_blocking=True)
+            d_hist.copy_(h_hist, non_blocking=True)
+            d_counts.copy_(h_counts, non_blocking=True)
+            d_count.copy_(h_count, non_blocking=True)
+            d_rng.copy_(h_rng, non_blocking=True)
+            s.sample_rows(d_logits, d_hist, d_counts, d_count, d_rng, out=d_tok)
+            h_tok.copy_(d_tok, non_blocking=True)
+
+        e2e_step(0)
+        sync_all()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(main_stream)
+        for i in range(args.e2e_steps):
+            e2e_step(i)
+        b.record(main_stream)
+        torch.cuda.synchronize()
+        ems = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        h2d = (bufs[0][0].numel() * 2 + hist.numel() * 4 + counts.numel() * 4 + count.numel() * 4
+               + rng.numel() * 8)
+        e2e = {"value": world * B / (ems / args.e2e_steps / 1e3), "unit": "rows/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(B * 4),
+               "steps": args.e2e_steps, "path": "pinned host -> qs_sample_rows (C ABI) -> host"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_reference_sample()
+        except Exception as exc:  # report, do not fail the GPU measurement
+            cpu = {"value": None, "error": str(exc)}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": world * B, "rows_per_gpu": B,
+                   "vocab": V, "window": WINDOW, "seq_len": None,
+                   "parallelism": f"row-sharded x{world}, tokens gathered to rank 0",
+                   "l2": "inputs larger than L2: two 311 MB logit buffers used in turn"},
+        "e2e": e2e,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic,
+                     "kernel": "qs::row_kernel<bf16>", "kernel_ms": row_ms,
+                     "algorithmic_bytes_per_launch": B * ROW_BYTES, "peak_source": peak_kind,
+                     "step_hbm_frac": world * B * STEP_ROW_BYTES / (ms_step / 1e3) / 1e9 / hbm / world},
+        "kernel_ms_per_step": {k: pr[k] / args.steps for k in ("penalty_ms", "row_ms", "ties_ms", "emit_ms")},
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    s.free()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -154,6 +154,26 @@ QS_API int qs_sample_rows_debug(qs_sampler* s, const void* d_logits, qs_dtype dt
 QS_API int qs_sample_host(qs_sampler* s, const float* h_logits, int batch, int* h_tokens,
                    unsigned flags);
 
+/* Kernel timing for benchmarks.  With profiling on, every sampling call
+ * records CUDA events around each of its kernels on the caller's stream;
+ * qs_profile_read waits for them and returns the accumulated device time per
+ * kernel and the launch counts since the last qs_profile_reset.  Launch
+ * counts are kept whether or not profiling is on. */
+typedef struct {
+    double penalty_ms;   /* override-table kernel */
+    double row_ms;       /* fused row kernel (the HBM stream) */
+    double ties_ms;      /* exact tie-arrangement kernel */
+    double emit_ms;      /* token copy-out / history update */
+    long long calls;     /* sampling calls */
+    long long launches;  /* kernels launched by this library */
+    long long row_launches;
+    long long timed_calls; /* calls whose kernels were timed */
+} qs_profile;
+
+QS_API int qs_profile_enable(qs_sampler* s, int on);
+QS_API int qs_profile_reset(qs_sampler* s);
+QS_API int qs_profile_read(qs_sampler* s, qs_profile* out);
+
 /* Message for the last error on the calling thread ("" if none). */
 QS_API const char* qs_last_error(void);
 

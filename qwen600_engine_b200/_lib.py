@@ -29,7 +29,7 @@ EXPORTS = (
     "qs_build_sampler", "qs_free_sampler", "qs_set_params", "qs_get_params",
     "qs_set_rng_state", "qs_get_rng_state", "qs_reset_sampler_history", "qs_sample",
     "qs_sample_rows", "qs_sample_rows_debug", "qs_sample_host", "qs_last_error",
-    "qs_max_vocab",
+    "qs_max_vocab", "qs_profile_enable", "qs_profile_reset", "qs_profile_read",
 )
 
 
@@ -44,6 +44,12 @@ class RowDebug(C.Structure):
                 ("n_minp", C.c_int), ("n_final", C.c_int), ("draw_pos", C.c_int),
                 ("exact_ties", C.c_int), ("sum_fallback", C.c_int), ("max_logit", C.c_float),
                 ("sum", C.c_float), ("r", C.c_float), ("renorm_sum", C.c_float)]
+
+
+class Profile(C.Structure):
+    _fields_ = [("penalty_ms", C.c_double), ("row_ms", C.c_double), ("ties_ms", C.c_double),
+                ("emit_ms", C.c_double), ("calls", C.c_longlong), ("launches", C.c_longlong),
+                ("row_launches", C.c_longlong), ("timed_calls", C.c_longlong)]
 
 
 ROW_DEBUG_FIELDS = [f for f, _ in RowDebug._fields_]
@@ -75,6 +81,9 @@ def _load() -> C.CDLL:
     lib.qs_sample_rows_debug.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, vp, vp,
                                          vp, vp, vp, i32, vp, u32]
     lib.qs_sample_host.argtypes = [vp, vp, i32, vp, u32]
+    lib.qs_profile_enable.argtypes = [vp, i32]
+    lib.qs_profile_reset.argtypes = [vp]
+    lib.qs_profile_read.argtypes = [vp, P(Profile)]
     lib.qs_last_error.restype = C.c_char_p
     lib.qs_last_error.argtypes = []
     lib.qs_max_vocab.argtypes = []

@@ -97,6 +97,46 @@ struct qs_sampler {
     uint32_t* exp_off = nullptr;
     uint32_t* exp_ent = nullptr;
     ExpFix fix() const { return ExpFix{exp_off, exp_ent, (uint32_t)QS_EXP_NB}; }
+    // launch accounting and optional per-kernel event timing
+    bool profiling = false;
+    qs_profile prof{};
+    struct Timed { int kind; cudaEvent_t a, b; };
+    std::vector<Timed> pending;
+    std::vector<cudaEvent_t> event_pool;
+};
+
+static cudaEvent_t take_event(qs_sampler* s) {
+    if (!s->event_pool.empty()) {
+        cudaEvent_t e = s->event_pool.back();
+        s->event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Brackets one kernel launch: records start/stop events when profiling.
+struct KernelScope {
+    qs_sampler* s;
+    int kind;
+    cudaStream_t st;
+    cudaEvent_t a = nullptr;
+    KernelScope(qs_sampler* s_, int kind_, cudaStream_t st_) : s(s_), kind(kind_), st(st_) {
+        s->prof.launches++;
+        if (kind == 1) s->prof.row_launches++;
+        if (s->profiling) {
+            a = take_event(s);
+            cudaEventRecord(a, st);
+        }
+    }
+    ~KernelScope() {
+        if (a) {
+            cudaEvent_t b = take_event(s);
+            cudaEventRecord(b, st);
+            s->pending.push_back({kind, a, b});
+        }
+    }
 };
 
 static void release(qs_sampler* s) {
@@ -109,6 +149,8 @@ static void release(qs_sampler* s) {
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
+    for (auto e : s->event_pool) cudaEventDestroy(e);
     if (s->stream) cudaStreamDestroy(s->stream);
     cudaSetDevice(prev);
     delete s;
@@ -329,7 +371,10 @@ static int run(qs_sampler* s, const Call& c) {
     const bool penalties = c.hist && c.hist_stride > 0 &&
                            (p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f ||
                             p.presence_penalty != 0.0f);
+    s->prof.calls++;
+    if (s->profiling) s->prof.timed_calls++;
     if (penalties) {
+        KernelScope ks(s, 0, c.stream);
         float* wb = (c.flags & QS_FLAG_WRITE_PENALIZED) ? (float*)c.logits : nullptr;
         if (c.dtype == QS_F32) {
             CK(launch_penalty<float>((const float*)c.logits, B, V, c.hist, c.hist_stride,
@@ -348,6 +393,8 @@ static int run(qs_sampler* s, const Call& c) {
     const int* ovn = penalties ? s->ov_n : nullptr;
     CK(cudaMemsetAsync(s->slow_count, 0, sizeof(int), c.stream));
     RowParams rp{p.temperature, p.topp, p.minp, p.top_k, c.flags};
+    {
+    KernelScope ks(s, 1, c.stream);
     if (c.dtype == QS_F32) {
         CK(launch_row_kernel<float>((const float*)c.logits, B, V, rp, ovn, s->ov_idx, s->ov_val,
                                     s->ov_stride, c.rng, s->res, s->slow_list, s->slow_count,
@@ -358,7 +405,9 @@ static int run(qs_sampler* s, const Call& c) {
                                             s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
                                             c.cand_cap, s->fix(), c.stream));
     }
+    }
     if (!greedy && topk && !(c.flags & QS_FLAG_INDEX_TIES)) {
+        KernelScope ks(s, 2, c.stream);
         TieParams tp{p.temperature, p.topp, p.minp, p.top_k};
         const int nct = B < s->tie_ctas ? B : s->tie_ctas;
         if (c.dtype == QS_F32) {
@@ -374,6 +423,7 @@ static int run(qs_sampler* s, const Call& c) {
         }
     }
     if (c.probs) {
+        KernelScope ks(s, 4, c.stream);
         if (c.dtype == QS_F32)
             CK(launch_probs<float>((const float*)c.logits, B, V, ovn, s->ov_idx, s->ov_val,
                                    s->ov_stride, s->res, c.probs, s->fix(), c.stream));
@@ -381,8 +431,11 @@ static int run(qs_sampler* s, const Call& c) {
             CK(launch_probs<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, ovn, s->ov_idx,
                                            s->ov_val, s->ov_stride, s->res, c.probs, s->fix(), c.stream));
     }
-    CK(launch_emit(B, V, s->window, s->res, c.tokens, c.dbg, c.ring, c.hcount, c.hpos,
-                   c.token_counts, c.stream));
+    {
+        KernelScope ks(s, 3, c.stream);
+        CK(launch_emit(B, V, s->window, s->res, c.tokens, c.dbg, c.ring, c.hcount, c.hpos,
+                       c.token_counts, c.stream));
+    }
     return QS_OK;
 }
 
@@ -432,6 +485,46 @@ int qs_sample_rows(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batc
     return qs_sample_rows_debug(s, d_logits, dtype, batch, vocab, d_hist, d_hist_counts,
                                 d_hist_count, window, d_rng, d_tokens, nullptr, nullptr, nullptr,
                                 nullptr, 0, stream, flags);
+}
+
+int qs_profile_enable(qs_sampler* s, int on) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    s->profiling = on != 0;
+    return QS_OK;
+}
+
+int qs_profile_reset(qs_sampler* s) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    DeviceGuard dg(s->device);
+    for (auto& t : s->pending) {
+        cudaEventSynchronize(t.b);
+        s->event_pool.push_back(t.a);
+        s->event_pool.push_back(t.b);
+    }
+    s->pending.clear();
+    s->prof = qs_profile{};
+    return QS_OK;
+}
+
+int qs_profile_read(qs_sampler* s, qs_profile* out) {
+    g_err.clear();
+    if (!s || !out) return fail(QS_ERR_INVALID, "NULL argument");
+    DeviceGuard dg(s->device);
+    for (auto& t : s->pending) {
+        CK(cudaEventSynchronize(t.b));
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, t.a, t.b));
+        double* dst = t.kind == 0 ? &s->prof.penalty_ms : t.kind == 1 ? &s->prof.row_ms
+                    : t.kind == 2 ? &s->prof.ties_ms : &s->prof.emit_ms;
+        if (t.kind != 4) *dst += ms;
+        s->event_pool.push_back(t.a);
+        s->event_pool.push_back(t.b);
+    }
+    s->pending.clear();
+    *out = s->prof;
+    return QS_OK;
 }
 
 int qs_sample_host(qs_sampler* s, const float* h_logits, int batch, int* h_tokens, unsigned flags) {

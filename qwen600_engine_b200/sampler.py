@@ -205,6 +205,18 @@ class Sampler:
             res["cand_prob"] = cp
         return res
 
+    # -- kernel timing (for benchmarks)
+    def profile(self, on: bool = True) -> None:
+        check(_lib.lib.qs_profile_enable(self._h, 1 if on else 0))
+
+    def profile_reset(self) -> None:
+        check(_lib.lib.qs_profile_reset(self._h))
+
+    def profile_read(self) -> Dict[str, float]:
+        p = _lib.Profile()
+        check(_lib.lib.qs_profile_read(self._h, C.byref(p)))
+        return {f: getattr(p, f) for f, _ in _lib.Profile._fields_}
+
     def reset_history(self) -> None:
         check(_lib.lib.qs_reset_sampler_history(self._h))
 
