@@ -24,11 +24,10 @@ cudaError_t launch_penalty(const T*, int, int, const int*, int, const int*, cons
                           const float*, float, float, float, int*, int*, float*, int, float*,
                           cudaStream_t);
 
-size_t row_kernel_smem(int V, int dtype_bytes, int ov_stride);
 template <typename T>
 cudaError_t launch_row_kernel(const T*, int, int, RowParams, const int*, const int*, const float*,
                               int, unsigned long long*, RowResult*, int*, int*, int*, float*, int,
-                              ExpFix, cudaStream_t);
+                              ExpFix, cudaStream_t, long long* phase_cycles = nullptr);
 template <typename T>
 cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
                                const int*, const int*, RowResult*, unsigned long long*, int*, int,
@@ -96,7 +95,8 @@ struct qs_sampler {
     // expf correction table on the device
     uint32_t* exp_off = nullptr;
     uint32_t* exp_ent = nullptr;
-    ExpFix fix() const { return ExpFix{exp_off, exp_ent, (uint32_t)QS_EXP_NB}; }
+    uint32_t* exp_bloom = nullptr;
+    ExpFix fix() const { return ExpFix{exp_off, exp_ent, exp_bloom, (uint32_t)QS_EXP_NB}; }
     // launch accounting and optional per-kernel event timing
     bool profiling = false;
     qs_profile prof{};
@@ -139,6 +139,19 @@ struct KernelScope {
     }
 };
 
+// Hash filter over the expf correction table (one bit per hashed entry).
+static const std::vector<uint32_t>& exp_bloom_host() {
+    static std::vector<uint32_t> bits = [] {
+        std::vector<uint32_t> b((size_t)1 << (kBloomBits - 5), 0u);
+        for (size_t i = 0; i < QS_EXP_NENT; i++) {
+            const uint32_t h = exp_fix_hash(qs_exp_fix_ent[i] & 0x7FFFFFFFu);
+            b[h >> 5] |= 1u << (h & 31);
+        }
+        return b;
+    }();
+    return bits;
+}
+
 static void release(qs_sampler* s) {
     if (!s) return;
     int prev = 0;
@@ -146,7 +159,7 @@ static void release(qs_sampler* s) {
     cudaSetDevice(s->device);
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts,
-                    s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent};
+                    s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
@@ -231,6 +244,7 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     ALLOC(s->d_tok, sizeof(int) * B);
     ALLOC(s->exp_off, sizeof(qs_exp_fix_off));
     ALLOC(s->exp_ent, sizeof(qs_exp_fix_ent));
+    ALLOC(s->exp_bloom, sizeof(uint32_t) << (kBloomBits - 5));
     if (W > 0) {
         ALLOC(s->ring, sizeof(int) * B * W);
         ALLOC(s->hcount, sizeof(int) * B);
@@ -250,6 +264,11 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
         e = cudaMemcpy(s->exp_off, qs_exp_fix_off, sizeof(qs_exp_fix_off), cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
         e = cudaMemcpy(s->exp_ent, qs_exp_fix_ent, sizeof(qs_exp_fix_ent), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        const std::vector<uint32_t>& bloom = exp_bloom_host();
+        e = cudaMemcpy(s->exp_bloom, bloom.data(), sizeof(uint32_t) * bloom.size(),
+                       cudaMemcpyHostToDevice);
+    }
     if (e == cudaSuccess && W > 0) {
         e = cudaMemset(s->hcount, 0, sizeof(int) * B);
         if (e == cudaSuccess) e = cudaMemset(s->hpos, 0, sizeof(int) * B);

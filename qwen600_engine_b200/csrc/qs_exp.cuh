@@ -11,18 +11,27 @@
 namespace qs {
 
 struct ExpFix {
-    const uint32_t* off;  // [nb + 1] bucket offsets
-    const uint32_t* ent;  // |x| bits, bit 31 set when expf = qs_exp_rn + 1 ulp
+    const uint32_t* off;    // [nb + 1] bucket offsets
+    const uint32_t* ent;    // |x| bits, bit 31 set when expf = qs_exp_rn + 1 ulp
+    const uint32_t* bloom;  // [1 << (kBloomBits - 5)] words: hash of every entry
     uint32_t nb;
 };
 
-__device__ __forceinline__ float ref_expf(float x, const ExpFix& fx) {
-    const float m = qs_exp_rn(x);
+constexpr int kBloomBits = 24;  // 2 MB filter: ~0.6% false positives for ~97k entries
+
+__host__ __device__ __forceinline__ uint32_t exp_fix_hash(uint32_t a) {
+    return (a * 0x9E3779B1u) >> (32 - kBloomBits);
+}
+
+// qs_exp_rn(x) corrected to the host libm's expf; m = qs_exp_rn(x) precomputed.
+static __device__ __noinline__ float ref_expf_fix(float x, float m, const ExpFix& fx) {
     uint32_t a = __float_as_uint(x);
     if (!(a & 0x80000000u)) return m;
     a &= 0x7FFFFFFFu;
     const uint32_t b = a >> 16;
     if (b >= fx.nb) return m;
+    const uint32_t h = exp_fix_hash(a);
+    if (!((__ldg(fx.bloom + (h >> 5)) >> (h & 31)) & 1u)) return m;
     uint32_t lo = __ldg(fx.off + b);
     const uint32_t end = __ldg(fx.off + b + 1);
     uint32_t hi = end;
@@ -39,6 +48,15 @@ __device__ __forceinline__ float ref_expf(float x, const ExpFix& fx) {
         }
     }
     return m;
+}
+
+static __device__ __forceinline__ float ref_expf(float x, const ExpFix& fx) {
+    return ref_expf_fix(x, qs_exp_rn(x), fx);
+}
+
+// One ulp of a finite non-negative float (distance to the next float up).
+__device__ __forceinline__ float ulp_up(float m) {
+    return __fsub_rn(__uint_as_float(__float_as_uint(m) + 1u), m);
 }
 
 }  // namespace qs

@@ -6,9 +6,13 @@
 // equality (sampler.h:75-94), then sorts those k with glibc's stable qsort
 // (sampler.h:214).  Among equal probabilities the result is an arrangement
 // left by the partition swaps, so this pass materialises the row's
-// (probability, index) array exactly as sample() builds it
-// (sampler.h:196-207) and replays every partition round with a parallel,
-// bit-identical formulation of the serial scans:
+// (value, index) array in the order sample() builds it (sampler.h:196-207)
+// and replays every partition round with a parallel, bit-identical
+// formulation of the serial scans.  The array holds order keys of the scaled
+// logits t rather than the probabilities p = g(t): g is monotone, so
+// "p <= P" is "t <= t_hi" and "p >= P" is "t >= t_lo" for the interval
+// [t_lo, t_hi] of scaled logits whose probability equals the pivot's, which
+// is found exactly per round with a few evaluations of g.  Scans:
 //
 //   L = positions whose value <= pivot (where the left scan stops), ascending
 //   R = positions whose value >= pivot (where the right scan stops), descending
@@ -67,10 +71,11 @@ __device__ __forceinline__ int tie_sum(int v, int* red) {
 
 __device__ __forceinline__ uint32_t pbits(unsigned long long a) { return (uint32_t)(a >> 32); }
 
-// One round of the reference's partition loop on A[lo..hi] with pivot bits P.
+// One round of the reference's partition loop on A[lo..hi]; the pivot's
+// probability is that of every key in [klo, khi].
 // Returns the scans' final (i, j) in *oi / *oj (valid in every thread).
-__device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t P, int* posL,
-                                int* posR, int* red, int* sh, int* oi, int* oj) {
+__device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t klo, uint32_t khi,
+                                int* posL, int* posR, int* red, int* sh, int* oi, int* oj) {
     const int tid = threadIdx.x;
     const int n = hi - lo + 1;
     const int per = (n + kTieThreads - 1) / kTieThreads;
@@ -79,8 +84,8 @@ __device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t 
     int cl = 0, cr = 0;
     for (int q = c0; q < c1; q++) {
         uint32_t v = pbits(A[q]);
-        cl += (v <= P);
-        cr += (v >= P);
+        cl += (v <= khi);
+        cr += (v >= klo);
     }
     int totL, totR;
     const int baseL = tie_excl_scan(cl, red, &totL);
@@ -90,7 +95,7 @@ __device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t 
     int nswap = 0;
     for (int q = c0; q < c1; q++) {
         uint32_t v = pbits(A[q]);
-        const bool isL = v <= P, isR = v >= P;
+        const bool isL = v <= khi, isR = v >= klo;
         if (isL) {
             aL++;
             posL[aL - 1] = q;
@@ -134,6 +139,36 @@ __device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t 
     *oi = sh[0];
     *oj = sh[1];
     __syncthreads();
+}
+
+// The reference's probability of a scaled logit t (sampler.h:197-206).
+__device__ __forceinline__ float prob_of(float t, const RowResult& rr, const ExpFix& fx) {
+    return __fmul_rn(ref_expf(__fsub_rn(t, rr.max_logit), fx), rr.sum_inv);
+}
+
+// [klo, khi]: the order keys of all t with prob_of(t) == prob_of(pivot).
+// prob_of is monotone non-decreasing, so both ends are found by galloping
+// from the pivot's key and bisecting (at most ~64 evaluations, usually 2).
+__device__ void prob_key_interval(uint32_t kp, const RowResult& rr, const ExpFix& fx,
+                                  uint32_t* klo, uint32_t* khi) {
+    const float P = prob_of(fkey_inv(kp), rr, fx);
+    auto same = [&](uint32_t k) {
+        const float t = fkey_inv(k);
+        return t == t && prob_of(t, rr, fx) == P;
+    };
+    if (!(P == P)) { *klo = kp; *khi = kp; return; }
+    // upward
+    uint32_t good = kp, step = 1;
+    while (good < 0xFFFFFFFFu - step && same(good + step)) { good += step; step <<= 1; }
+    uint32_t bad = (good < 0xFFFFFFFFu - step) ? good + step : 0xFFFFFFFFu;
+    while (bad - good > 1) { const uint32_t mid = good + (bad - good) / 2; if (same(mid)) good = mid; else bad = mid; }
+    *khi = good;
+    // downward
+    good = kp; step = 1;
+    while (good > step && same(good - step)) { good -= step; step <<= 1; }
+    bad = (good > step) ? good - step : 0u;
+    while (good - bad > 1) { const uint32_t mid = bad + (good - bad) / 2; if (same(mid)) good = mid; else bad = mid; }
+    *klo = good;
 }
 
 __device__ void tie_sort_desc(unsigned long long* a, int n) {
@@ -183,7 +218,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             ovv[i] = ov_val[(size_t)row * ov_stride + i];
         }
         __syncthreads();
-        // probindex as sample() leaves it before selection (sampler.h:195-207)
+        // the row's values in index order, as order keys of t (sampler.h:184-201)
         for (int i = tid; i < V; i += kTieThreads) {
             float l = Elem<T>::widen(L[i]);
             if (nov) {
@@ -191,10 +226,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                 while (lo < hi) { int m = (lo + hi) >> 1; if (ovi[m] < i) lo = m + 1; else hi = m; }
                 if (lo < nov && ovi[lo] == i) l = ovv[lo];
             }
-            const float t = __fmul_rn(l, rr.inv_temp);
-            const float e = ref_expf(__fsub_rn(t, rr.max_logit), fx);
-            const float p = __fmul_rn(e, rr.sum_inv);
-            A[i] = ((unsigned long long)__float_as_uint(p) << 32) | (unsigned)i;
+            A[i] = ((unsigned long long)fkey(__fmul_rn(l, rr.inv_temp)) << 32) | (unsigned)i;
         }
         __syncthreads();
         // quick_select(probindex, V, k - 1)  (sampler.h:76-94)
@@ -203,13 +235,27 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
         long long rounds = 0;
         const long long max_rounds = 4ll * V + 64;  // the serial loop needs far fewer
         while (lo < hi && rounds++ < max_rounds) {
-            const uint32_t P = pbits(A[kk]);
+            if (tid == 0) {
+                const uint32_t kp = pbits(A[kk]);
+                uint32_t klo, khi;
+                prob_key_interval(kp, rr, fx, &klo, &khi);
+                sh[2] = (int)klo;
+                sh[3] = (int)khi;
+            }
             __syncthreads();
+            const uint32_t klo = (uint32_t)sh[2], khi = (uint32_t)sh[3];
             int i, j;
-            partition_round(A, lo, hi, P, posL, posR, red, sh, &i, &j);
+            partition_round(A, lo, hi, klo, khi, posL, posR, red, sh, &i, &j);
             if (j < kk) lo = i;
             if (i > kk) hi = j;
         }
+        // exact probabilities of the k selected entries (sampler.h:197-206)
+        for (int i = tid; i < k; i += kTieThreads) {
+            const float t = fkey_inv(pbits(A[i]));
+            const float p = __fmul_rn(ref_expf(__fsub_rn(t, rr.max_logit), fx), rr.sum_inv);
+            A[i] = ((unsigned long long)__float_as_uint(p) << 32) | (A[i] & 0xFFFFFFFFull);
+        }
+        __syncthreads();
         // stable qsort of the first k by probability, descending (sampler.h:214)
         int npow = 1;
         while (npow < k) npow <<= 1;
