@@ -29,6 +29,7 @@ namespace qs {
 
 constexpr int kTieThreads = 1024;
 constexpr int kTieWarps = kTieThreads / 32;
+constexpr int kTieSmemRange = 4096;  // active ranges up to this size continue in shared memory
 
 __device__ __forceinline__ int tie_excl_scan(int v, int* red, int* total) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -56,6 +57,35 @@ __device__ __forceinline__ int tie_excl_scan(int v, int* red, int* total) {
     return before + x - v;
 }
 
+// Exclusive block scan of two ints at once (one value per warp, held in lane
+// 0); returns both offsets and totals.
+__device__ __forceinline__ void tie_excl_scan2(int a, int b, int* red, int* oa, int* ob, int* ta,
+                                               int* tb) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) { red[w] = a; red[32 + w] = b; }
+    __syncthreads();
+    if (w == 0) {
+        int x = lane < kTieWarps ? red[lane] : 0;
+        int y = lane < kTieWarps ? red[32 + lane] : 0;
+        int ix = x, iy = y;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, ix, o);
+            const int v = __shfl_up_sync(0xffffffffu, iy, o);
+            if (lane >= o) { ix += u; iy += v; }
+        }
+        red[64 + lane] = ix - x;
+        red[96 + lane] = iy - y;
+        if (lane == 31) { red[128] = ix; red[129] = iy; }
+    }
+    __syncthreads();
+    *oa = red[64 + w];
+    *ob = red[96 + w];
+    *ta = red[128];
+    *tb = red[129];
+}
+
 __device__ __forceinline__ int tie_sum(int v, int* red) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
@@ -72,48 +102,83 @@ __device__ __forceinline__ int tie_sum(int v, int* red) {
 __device__ __forceinline__ uint32_t pbits(unsigned long long a) { return (uint32_t)(a >> 32); }
 
 // One round of the reference's partition loop on A[lo..hi]; the pivot's
-// probability is that of every key in [klo, khi].
+// probability is that of every key in [klo, khi].  Each warp owns a
+// contiguous chunk of the range and walks it 32 entries at a time (coalesced
+// loads); inclusive ranks come from ballots, chunk offsets from a block scan.
 // Returns the scans' final (i, j) in *oi / *oj (valid in every thread).
 __device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t klo, uint32_t khi,
                                 int* posL, int* posR, int* red, int* sh, int* oi, int* oj) {
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n = hi - lo + 1;
-    const int per = (n + kTieThreads - 1) / kTieThreads;
-    const int c0 = lo + tid * per;
+    const int per = (n + kTieWarps - 1) / kTieWarps;
+    const int c0 = lo + warp * per;
     const int c1 = min(c0 + per, hi + 1);
+    const unsigned lt = (1u << lane) - 1u;
+    constexpr int UN = 8;  // loads in flight per lane
     int cl = 0, cr = 0;
-    for (int q = c0; q < c1; q++) {
-        uint32_t v = pbits(A[q]);
-        cl += (v <= khi);
-        cr += (v >= klo);
+    for (int q0 = c0; q0 < c1; q0 += 32 * UN) {
+        uint32_t v[UN];
+#pragma unroll
+        for (int u = 0; u < UN; u++) {
+            const int q = q0 + u * 32 + lane;
+            v[u] = (q < c1) ? pbits(A[q]) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < UN; u++) {
+            const int q = q0 + u * 32 + lane;
+            cl += __popc(__ballot_sync(0xffffffffu, q < c1 && v[u] <= khi));
+            cr += __popc(__ballot_sync(0xffffffffu, q < c1 && v[u] >= klo));
+        }
     }
-    int totL, totR;
-    const int baseL = tie_excl_scan(cl, red, &totL);
-    const int baseR = tie_excl_scan(cr, red, &totR);
-    int aL = baseL;
-    int rAfter = totR - baseR;  // #R in [c0, hi]
+    int baseL, baseR, totL, totR;
+    tie_excl_scan2(cl, cr, red, &baseL, &baseR, &totL, &totR);
+    int aL = baseL;   // #L before this step
+    int bB = baseR;   // #R before this step
     int nswap = 0;
-    for (int q = c0; q < c1; q++) {
-        uint32_t v = pbits(A[q]);
-        const bool isL = v <= khi, isR = v >= klo;
+    for (int q0 = c0; q0 < c1; q0 += 32 * UN) {
+      uint32_t vv[UN];
+#pragma unroll
+      for (int u = 0; u < UN; u++) {
+          const int q = q0 + u * 32 + lane;
+          vv[u] = (q < c1) ? pbits(A[q]) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < UN; u++) {
+        const int q = q0 + u * 32 + lane;
+        const bool in = q < c1;
+        const uint32_t v = vv[u];
+        const bool isL = in && v <= khi, isR = in && v >= klo;
+        const unsigned bl = __ballot_sync(0xffffffffu, isL);
+        const unsigned br = __ballot_sync(0xffffffffu, isR);
+        const int a = aL + __popc(bl & lt) + 1;          // #L in [lo, q]
+        const int b = totR - bB - __popc(br & lt);      // #R in [q, hi]
         if (isL) {
-            aL++;
-            posL[aL - 1] = q;
-            if (rAfter >= aL) nswap++;
+            posL[a - 1] = q;
+            nswap += (b >= a);
         }
-        if (isR) {
-            posR[rAfter - 1] = q;
-            rAfter--;
-        }
+        if (isR) posR[b - 1] = q;
+        aL += __popc(bl);
+        bB += __popc(br);
+      }
     }
     const int T = tie_sum(nswap, red);
     __syncthreads();  // posL / posR complete
-    for (int t = tid; t < T; t += kTieThreads) {
-        const int x = posL[t], y = posR[t];
-        if (x != y) {
-            unsigned long long a = A[x];
-            A[x] = A[y];
-            A[y] = a;
+    for (int t0 = tid; t0 < T; t0 += 4 * kTieThreads) {
+        int x[4], y[4];
+        unsigned long long ax[4], ay[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int t = t0 + u * kTieThreads;
+            x[u] = (t < T) ? posL[t] : -1;
+            y[u] = (t < T) ? posR[t] : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (x[u] >= 0 && x[u] != y[u]) { ax[u] = A[x[u]]; ay[u] = A[y[u]]; }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (x[u] >= 0 && x[u] != y[u]) { A[x[u]] = ay[u]; A[y[u]] = ax[u]; }
         }
     }
     if (tid == 0) {
@@ -194,11 +259,12 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             RowResult* __restrict__ res, unsigned long long* __restrict__ scratch,
             int* __restrict__ pos_scratch, int* __restrict__ cand_index_out,
             float* __restrict__ cand_prob_out, int cand_cap, ExpFix fx) {
-    __shared__ int red[32];
+    __shared__ int red[160];
     __shared__ int sh[4];
-    __shared__ unsigned long long sk[kCandCap];
-    extern __shared__ unsigned char dyn[];
-    int* ovi = reinterpret_cast<int*>(dyn);
+    extern __shared__ __align__(16) unsigned char dyn[];
+    unsigned long long* sA = reinterpret_cast<unsigned long long*>(dyn);   // [kTieSmemRange]
+    unsigned long long* sk = sA + kTieSmemRange;                           // [kCandCap]
+    int* ovi = reinterpret_cast<int*>(sk + kCandCap);
     float* ovv = reinterpret_cast<float*>(ovi + (ov_stride > 0 ? ov_stride : 1));
 
     const int tid = threadIdx.x;
@@ -220,23 +286,31 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
         __syncthreads();
         // the row's values in index order, as order keys of t (sampler.h:184-201)
         for (int i = tid; i < V; i += kTieThreads) {
-            float l = Elem<T>::widen(L[i]);
-            if (nov) {
-                int lo = 0, hi = nov;
-                while (lo < hi) { int m = (lo + hi) >> 1; if (ovi[m] < i) lo = m + 1; else hi = m; }
-                if (lo < nov && ovi[lo] == i) l = ovv[lo];
-            }
+            const float l = Elem<T>::widen(L[i]);
             A[i] = ((unsigned long long)fkey(__fmul_rn(l, rr.inv_temp)) << 32) | (unsigned)i;
         }
+        __syncthreads();
+        for (int j = tid; j < nov; j += kTieThreads)
+            A[ovi[j]] = ((unsigned long long)fkey(__fmul_rn(ovv[j], rr.inv_temp)) << 32) | (unsigned)ovi[j];
         __syncthreads();
         // quick_select(probindex, V, k - 1)  (sampler.h:76-94)
         int lo = 0, hi = V - 1;
         const int kk = k - 1;
         long long rounds = 0;
         const long long max_rounds = 4ll * V + 64;  // the serial loop needs far fewer
+        unsigned long long* W = A;  // the array the rounds work on
+        int woff = 0, wn = 0;       // W[q - woff] holds position q, for wn positions
         while (lo < hi && rounds++ < max_rounds) {
+            if (W == A && hi - lo + 1 <= kTieSmemRange) {
+                // continue in shared memory; positions outside [lo, hi] never move again
+                for (int q = lo + tid; q <= hi; q += kTieThreads) sA[q - lo] = A[q];
+                __syncthreads();
+                W = sA;
+                woff = lo;
+                wn = hi - lo + 1;
+            }
             if (tid == 0) {
-                const uint32_t kp = pbits(A[kk]);
+                const uint32_t kp = pbits(W[kk - woff]);
                 uint32_t klo, khi;
                 prob_key_interval(kp, rr, fx, &klo, &khi);
                 sh[2] = (int)klo;
@@ -245,9 +319,14 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             __syncthreads();
             const uint32_t klo = (uint32_t)sh[2], khi = (uint32_t)sh[3];
             int i, j;
-            partition_round(A, lo, hi, klo, khi, posL, posR, red, sh, &i, &j);
+            partition_round(W - woff, lo, hi, klo, khi, posL, posR, red, sh, &i, &j);
             if (j < kk) lo = i;
             if (i > kk) hi = j;
+        }
+        if (W != A) {
+            // write the shared-memory range back
+            for (int q = tid; q < wn; q += kTieThreads) A[woff + q] = sA[q];
+            __syncthreads();
         }
         // exact probabilities of the k selected entries (sampler.h:197-206)
         for (int i = tid; i < k; i += kTieThreads) {
@@ -330,7 +409,11 @@ cudaError_t launch_ties_kernel(const T* logits, int V, TieParams prm, const int*
                                unsigned long long* scratch, int* pos_scratch, int nctas,
                                int* cand_index, float* cand_prob, int cand_cap, ExpFix fx,
                                cudaStream_t stream) {
-    const size_t smem = 8 * (size_t)(ov_stride > 0 ? ov_stride : 1) + 16;
+    const size_t smem = 8 * (size_t)kTieSmemRange + 8 * (size_t)kCandCap +
+                        8 * (size_t)(ov_stride > 0 ? ov_stride : 1) + 16;
+    cudaError_t err = cudaFuncSetAttribute(ties_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err != cudaSuccess) return err;
     ties_kernel<T><<<nctas, kTieThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val,
                                                          ov_stride, slow_list, slow_count, res,
                                                          scratch, pos_scratch, cand_index,
