@@ -31,7 +31,8 @@ cudaError_t launch_row_kernel(const T*, int, int, RowParams, const int*, const i
 template <typename T>
 cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
                                const int*, const int*, RowResult*, unsigned long long*, int*, int,
-                               int*, float*, int, ExpFix, cudaStream_t);
+                               int*, float*, int, ExpFix, cudaStream_t,
+                               long long* phase_cycles = nullptr);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, cudaStream_t);
 template <typename T>
@@ -190,6 +191,12 @@ struct DeviceGuard {
 };
 
 extern "C" {
+
+// Lets the fixed-memory entry point (qs_static.cu) report through qs_last_error.
+int qs_static_last_error_set(const char* msg) {
+    g_err = msg ? msg : "";
+    return 0;
+}
 
 const char* qs_last_error(void) { return g_err.c_str(); }
 

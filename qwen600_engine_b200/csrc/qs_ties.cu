@@ -258,7 +258,8 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             const int* __restrict__ slow_list, const int* __restrict__ slow_count,
             RowResult* __restrict__ res, unsigned long long* __restrict__ scratch,
             int* __restrict__ pos_scratch, int* __restrict__ cand_index_out,
-            float* __restrict__ cand_prob_out, int cand_cap, ExpFix fx) {
+            float* __restrict__ cand_prob_out, int cand_cap, ExpFix fx,
+            long long* __restrict__ phase_cycles) {
     __shared__ int red[160];
     __shared__ int sh[4];
     extern __shared__ __align__(16) unsigned char dyn[];
@@ -276,6 +277,8 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
 
     for (int li = blockIdx.x; li < nslow; li += gridDim.x) {
         const int row = slow_list[li];
+        long long* ph = phase_cycles ? phase_cycles + (size_t)li * 8 : nullptr;
+        if (ph && tid == 0) ph[0] = clock64();
         const RowResult rr = res[row];
         const T* L = logits + (size_t)row * V;
         const int nov = ov_n ? ov_n[row] : 0;
@@ -293,6 +296,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
         for (int j = tid; j < nov; j += kTieThreads)
             A[ovi[j]] = ((unsigned long long)fkey(__fmul_rn(ovv[j], rr.inv_temp)) << 32) | (unsigned)ovi[j];
         __syncthreads();
+        if (ph && tid == 0) ph[1] = clock64();
         // quick_select(probindex, V, k - 1)  (sampler.h:76-94)
         int lo = 0, hi = V - 1;
         const int kk = k - 1;
@@ -302,6 +306,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
         int woff = 0, wn = 0;       // W[q - woff] holds position q, for wn positions
         while (lo < hi && rounds++ < max_rounds) {
             if (W == A && hi - lo + 1 <= kTieSmemRange) {
+                if (ph && tid == 0) { ph[2] = clock64(); ph[6] = rounds; }
                 // continue in shared memory; positions outside [lo, hi] never move again
                 for (int q = lo + tid; q <= hi; q += kTieThreads) sA[q - lo] = A[q];
                 __syncthreads();
@@ -328,6 +333,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             for (int q = tid; q < wn; q += kTieThreads) A[woff + q] = sA[q];
             __syncthreads();
         }
+        if (ph && tid == 0) { ph[3] = clock64(); ph[7] = rounds; }
         // exact probabilities of the k selected entries (sampler.h:197-206)
         for (int i = tid; i < k; i += kTieThreads) {
             const float t = fkey_inv(pbits(A[i]));
@@ -380,6 +386,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                 cum = __fadd_rn(cum, __fmul_rn(P(i), inv2));
                 if (rr.r < cum) { pos = i; break; }
             }
+            if (ph) ph[4] = clock64();
             RowResult o = rr;
             o.token = I(pos);
             o.n_topk = k;
@@ -408,7 +415,7 @@ cudaError_t launch_ties_kernel(const T* logits, int V, TieParams prm, const int*
                                const int* slow_list, const int* slow_count, RowResult* res,
                                unsigned long long* scratch, int* pos_scratch, int nctas,
                                int* cand_index, float* cand_prob, int cand_cap, ExpFix fx,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, long long* phase_cycles) {
     const size_t smem = 8 * (size_t)kTieSmemRange + 8 * (size_t)kCandCap +
                         8 * (size_t)(ov_stride > 0 ? ov_stride : 1) + 16;
     cudaError_t err = cudaFuncSetAttribute(ties_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -417,19 +424,19 @@ cudaError_t launch_ties_kernel(const T* logits, int V, TieParams prm, const int*
     ties_kernel<T><<<nctas, kTieThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val,
                                                          ov_stride, slow_list, slow_count, res,
                                                          scratch, pos_scratch, cand_index,
-                                                         cand_prob, cand_cap, fx);
+                                                         cand_prob, cand_cap, fx, phase_cycles);
     return cudaGetLastError();
 }
 
 template cudaError_t launch_ties_kernel<float>(const float*, int, TieParams, const int*, const int*,
                                                const float*, int, const int*, const int*,
                                                RowResult*, unsigned long long*, int*, int, int*,
-                                               float*, int, ExpFix, cudaStream_t);
+                                               float*, int, ExpFix, cudaStream_t, long long*);
 template cudaError_t launch_ties_kernel<__nv_bfloat16>(const __nv_bfloat16*, int, TieParams,
                                                        const int*, const int*, const float*, int,
                                                        const int*, const int*, RowResult*,
                                                        unsigned long long*, int*, int, int*,
-                                                       float*, int, ExpFix, cudaStream_t);
+                                                       float*, int, ExpFix, cudaStream_t, long long*);
 
 // ------------------------------------------------------------- epilogue
 // Copies tokens out and, for the stateful API, records each row's token in
