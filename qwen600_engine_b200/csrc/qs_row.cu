@@ -10,31 +10,30 @@
 //     elements) keep the maximum (bf16 pairs compared packed).  Greedy rows
 //     (T < 1e-6, sampler.h:178) finish here: the first segment holding the
 //     row maximum is re-read and its lowest index returned (strict '>'
-//     argmax, sampler.h:100-111).
-//  B  temperature: t = l * (1/T) (sampler.h:184-187).  x -> fl(x*c) is
-//     monotone for c > 0, so segment maxima and the row maximum of t are
-//     fl(max_l * inv).  An exclusive prefix maximum over segments bounds the
-//     running softmax sum from below; an element with t < prefix - 17.5 adds
-//     less than half an ulp to it and cannot change the reference's
-//     sequential fp32 sum, so segments whose maximum is below that bound are
-//     skipped ("cold").
-//  C  exact softmax denominator.  The reference adds expf(t_i - max) in
-//     index order in fp32 (sampler.h:195-201).  Inside one binade
-//     [2^E, 2^(E+1)) every such addition is an integer increment on the grid
-//     u = 2^(E-23) (round to nearest even), so a run of additions is a
-//     transfer function of the incoming parity: two increments and two
-//     outgoing parities, composable associatively.  An approximate sum per
-//     hot segment predicts each segment's binade; segment functions are
-//     built in parallel; one warp walks the hot segments 32 at a time,
-//     composing functions with a warp scan while the running sum provably
-//     stays in the predicted binade, and handles the segments where it
-//     crosses a binade element by element (again with a warp scan between
-//     crossings).  Bit-identical to the serial sum.
-//  D  candidates: tau = k-th largest segment maximum (a lower bound of the
-//     k-th largest t, found by one warp with a 4-round radix select);
-//     elements with t >= tau are gathered, their probabilities
-//     p = fl(expf(t - max) * fl(1/sum)) formed as sampler.h:197-206 does and
-//     ranked by (p desc, index asc).
+//     argmax, sampler.h:100-111).  Other rows also stash, from registers,
+//     every element that may matter to the softmax sum: with t = l * (1/T)
+//     (sampler.h:184-187), an element with t below (maximum t of all earlier
+//     elements) - 17.5 adds less than half an ulp to the reference's running
+//     fp32 sum and cannot change it, so the stash keeps t >= lb - 17.5 for a
+//     lower bound lb of that prefix maximum (exact for the first 64 segments,
+//     afterwards the maxima seen so far of earlier segments).
+//  C  exact softmax denominator.  The reference adds expf(t_i - max) in index
+//     order in fp32 (sampler.h:195-201).  The stashed terms are formed in
+//     parallel, placed in index order and added sequentially; the skipped
+//     terms are exact no-ops, so the sum is bit-identical.  Rows whose stash
+//     overflows (flat distributions) use the dense method instead: inside
+//     one binade [2^E, 2^(E+1)) every addition is an integer increment on the
+//     grid u = 2^(E-23) (round to nearest even), so a run of additions is a
+//     transfer function of the incoming parity, composable associatively;
+//     hot segments are re-read and composed with warp scans, element by
+//     element where the sum crosses a binade.
+//  D  candidates.  The stash holds every element with t >= theta (the largest
+//     bound used, minus 17.5), so the reference's sorted list starts with the
+//     stashed elements above theta: all of its top-k when at least k exist.
+//     Their probabilities p = fl(expf(t - max) * fl(1/sum)) (sampler.h:197-206)
+//     are ranked by (p desc, index asc).  When min-p / top-p / the draw need
+//     positions an unstashed element could reach, the row re-reads the
+//     segments whose maximum reaches the k-th largest segment maximum.
 //  E  min-p (sampler.h:144-162), top-p (sampler.h:226-237), renormalise
 //     (sampler.h:240-243) and the CDF draw with the row's xorshift64*
 //     uniform (sampler.h:246-255), serially on the <= k survivors.  If the
@@ -43,15 +42,25 @@
 //     for qs_ties.cu.
 //
 // expf: the reference calls the host libm's expf; ref_expf reproduces it
-// (qs_exp.cuh).  Where a value only feeds a rounding decision, the cheaper
-// correctly rounded qs_exp_rn is used unless a one-ulp change of the value
-// could change that decision, in which case the correction is looked up.
+// (qs_exp.cuh).  In the dense method, where a value only feeds a rounding
+// decision, CUDA's expf decides unless a 4-ulp change of the value could
+// change that decision, in which case the exact value is formed.
 #include "qs_common.cuh"
 
 namespace qs {
 
 constexpr int kRowThreads = 256;
 constexpr int kRowWarps = kRowThreads / 32;
+#ifndef QS_ROW_MIN_BLOCKS
+#define QS_ROW_MIN_BLOCKS 3
+#endif
+#ifndef QS_ROW_ROUND
+#define QS_ROW_ROUND 64
+#endif
+constexpr int kRowMinBlocks = QS_ROW_MIN_BLOCKS;  // resident rows per SM the registers are sized for
+constexpr int kRowRound = QS_ROW_ROUND;  // segments per streaming round (kRowRound / 8 per warp)
+constexpr int kStashCap = 1536;          // stashed elements per row before the dense method
+static_assert((kRowRound == 32 || kRowRound == 64) && kRowRound % kRowWarps == 0, "round layout");
 constexpr int kRankSortMax = 512;  // candidates ranked by counting up to this many
 constexpr float kDelta = 1e-5f;    // binade prediction margin (misses only cost a replay)
 constexpr uint32_t kTwo24 = 1u << 24;
@@ -421,35 +430,25 @@ __device__ __noinline__ uint32_t block_kth_largest_row(const RowView<T>& rv, int
     return prefix;
 }
 
-// Sequential fp32 sum over an index-ordered list of exponent arguments d
-// (one warp): each lane evaluates CUDA's expf for one of the next 32 terms,
-// then lane 0 adds them in order, deciding each rounding on that value when
-// its whole 4-ulp band rounds alike and forming the reference's exact term
-// otherwise.
-__device__ float walk_list(const float* list, int n, float s, const ExpFix& fx) {
-    const int lane = threadIdx.x & 31;
-    for (int i0 = 0; i0 < n; i0 += 32) {
-        const int i = i0 + lane;
-        const float d = i < n ? list[i] : -INFINITY;
-        const float fast = i < n ? expf(d) : 0.0f;
-        const int m = min(32, n - i0);
-        for (int j = 0; j < m; j++) {
-            const float dj = __shfl_sync(0xffffffffu, d, j);
-            const float fj = __shfl_sync(0xffffffffu, fast, j);
-            const float r0 = __fadd_rn(s, fj);
-            const float b = band(fj > 0.0f ? fj : 1.4e-45f);
-            const bool same = (fj == fj) && __fadd_rn(s, fmaxf(__fsub_rn(fj, b), 0.0f)) == r0 &&
-                              __fadd_rn(s, __fadd_rn(fj, b)) == r0;
-            s = same ? r0 : __fadd_rn(s, exact_exp(dj, fx));
-        }
+// fl(...fl(fl(s + a[0]) + a[1]) ... + a[n-1]): the sequential fp32 sum of an
+// index-ordered array of terms, by one thread (a 16-byte aligned).
+__device__ __noinline__ float serial_sum(const float* a, int n, float s) {
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        const float4 x = *reinterpret_cast<const float4*>(a + i);
+        const float4 y = *reinterpret_cast<const float4*>(a + i + 4);
+        s = __fadd_rn(s, x.x); s = __fadd_rn(s, x.y); s = __fadd_rn(s, x.z); s = __fadd_rn(s, x.w);
+        s = __fadd_rn(s, y.x); s = __fadd_rn(s, y.y); s = __fadd_rn(s, y.z); s = __fadd_rn(s, y.w);
     }
+    for (; i < n; i++) s = __fadd_rn(s, a[i]);
     return s;
 }
 
 // Replays hot segment g element by element from running sum s (warp-wide;
-// returns the new sum).  Additions that keep the sum inside its binade are
-// composed with a warp scan; the lane whose elements leave the binade adds
-// them one at a time, then the scan resumes after it.
+// returns the new sum).  Each lane first forms the exact terms of its EPL
+// elements; additions that keep the sum inside its binade are then composed
+// with a warp scan, and the lane whose terms leave the binade adds them one at
+// a time before the scan resumes after it.
 template <typename T>
 __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float thr, float inv, float M,
                                            float s, const ExpFix& fx) {
@@ -457,25 +456,20 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
     const int lane = threadIdx.x & 31;
     float v[EPL];
     rv.load(g, lane, v);
-    float d[EPL], fe[EPL];
-    unsigned sig = 0;
+    float ex[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; e++) {
         const float t = __fmul_rn(v[e], inv);
-        d[e] = __fsub_rn(t, M);
-        const bool sg = t >= thr;
-        sig |= (sg ? 1u : 0u) << e;
-        fe[e] = sg ? expf(d[e]) : 0.0f;
+        ex[e] = (t >= thr) ? ref_expf(__fsub_rn(t, M), fx) : 0.0f;
     }
     int start = 0;  // lanes below `start` are already added
     while (start < 32) {
         const int E = sum_binade(s);
         const uint32_t S = sum_units(s, E);
         Tf f = tf_identity();
-        if (lane >= start && sig) {
+        if (lane >= start) {
 #pragma unroll
-            for (int e = 0; e < EPL; e++)
-                if ((sig >> e) & 1u) f = tf_compose(f, tf_element(grid_term(d[e], fe[e], E, fx), E));
+            for (int e = 0; e < EPL; e++) f = tf_compose(f, tf_element(ex[e], E));
         }
         const Tf pre = warp_scan_tf(f);
         const uint32_t inc = (S & 1u) ? pre.inc1 : pre.inc0;
@@ -487,173 +481,71 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
             break;
         }
         const int c = __ffs(bm) - 1;
-        // lanes start..c-1 stay inside the binade
         const uint32_t prev = __shfl_sync(0xffffffffu, inc, c > 0 ? c - 1 : 0);
-        const uint32_t before = (c > start) ? prev : 0u;
-        s = ldexpf((float)(S + before), E - 23);
-        // lane c, one element at a time
-        const unsigned sc = __shfl_sync(0xffffffffu, sig, c);
+        s = ldexpf((float)(S + ((c > start) ? prev : 0u)), E - 23);
 #pragma unroll
-        for (int e = 0; e < EPL; e++) {
-            const float de = __shfl_sync(0xffffffffu, d[e], c);
-            const float fc = __shfl_sync(0xffffffffu, fe[e], c);
-            if ((sc >> e) & 1u) s = add_term(s, de, fc, fx);
-        }
+        for (int e = 0; e < EPL; e++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, ex[e], c));
         start = c + 1;
     }
     return s;
 }
 
+// Shared-memory layout of one row, shared by the kernel and its launcher.
+struct RowSmem {
+    size_t segm, segk, segov, ovi, ovv, pubr, region, ct, ci, cp, so, ck, rhist, total;
+    int nseg, nrounds, scap, ccap;
+    __host__ __device__ static size_t r16(size_t b) { return (b + 15) & ~(size_t)15; }
+    __host__ __device__ RowSmem(int V, int seg, int ov_stride, int ccap_, int scap_) {
+        nseg = (V + seg - 1) / seg;
+        nrounds = (nseg + kRowRound - 1) / kRowRound;
+        scap = scap_;
+        ccap = ccap_;
+        const size_t ovs = (size_t)(ov_stride > 0 ? ov_stride : 1);
+        size_t p = 0;
+        segm = p; p += r16(4 * (size_t)nseg);
+        segk = p; p += r16(4 * (size_t)nseg);
+        segov = p; p += r16((size_t)nseg);
+        ovi = p; p += r16(4 * ovs);
+        ovv = p; p += r16(4 * ovs);
+        pubr = p; p += r16(4 * (size_t)nrounds);
+        region = p;
+        const size_t fast = 16 * (size_t)scap + 8 * (size_t)nseg;  // stash t, i, e, ordered terms; tables
+        const size_t slow = 32 * (size_t)nseg;                      // hot, hthr, hA, hE, Tf
+        p += r16(fast > slow ? fast : slow);
+        ct = p; p += r16(4 * (size_t)ccap);
+        ci = p; p += r16(4 * (size_t)ccap);
+        cp = p; p += r16(4 * (size_t)ccap);
+        so = p; p += r16(4 * (size_t)ccap);
+        ck = p; p += r16(8 * (size_t)ccap);
+        rhist = p; p += r16(4 * 256);
+        total = p;
+    }
+};
+
+// Scalars shared by the threads of one row.
+struct RowShared {
+    float red_f[32];
+    int red_i[32];
+    double red_d[32];
+    int misc[8];
+    int nhot, ncand, fb, ncseg, nst, ovf, done, nknown;
+    uint32_t maxlb;
+    float sum, r, tau;
+};
+
+// Dense rows (the stash overflowed): the exact sequential sum from the hot
+// segments, re-read from L2, with per-segment transfer functions.  Leaves the
+// sum in sh->sum.  segm holds the segment maxima of t.
 template <typename T>
-__global__ void __launch_bounds__(kRowThreads, 4)
-row_kernel(const T* __restrict__ logits, int V, RowParams prm,
-           const int* __restrict__ ov_n, const int* __restrict__ ov_idx,
-           const float* __restrict__ ov_val, int ov_stride,
-           unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
-           int* __restrict__ slow_list, int* __restrict__ slow_count,
-           int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
-           ExpFix fx, int ccap, long long* __restrict__ phase_cycles) {
-    constexpr int EPL = Elem<T>::kPerLane;
-    constexpr int SEG = 32 * EPL;
-    constexpr int U = 8;  // segments in flight per warp in the streaming pass
-    const int row = blockIdx.x;
+__device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* segm, float inv, float M,
+                                       unsigned char* region, RowShared* sh, ExpFix fx) {
+    constexpr int EPL = RowView<T>::EPL;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nseg = (V + SEG - 1) / SEG;
-
-    // ---- shared memory carve-up
-    extern __shared__ __align__(16) unsigned char smem[];
-    unsigned char* p = smem;
-    auto take = [&](size_t bytes) { unsigned char* q = p; p += (bytes + 15) & ~(size_t)15; return q; };
-    float* segm = (float*)take(sizeof(float) * nseg);            // segment maxima (l, then t)
-    uint32_t* segk = (uint32_t*)take(sizeof(uint32_t) * nseg);   // order keys of segm
-    unsigned char* segov = take(nseg);
-    int* hot = (int*)take(sizeof(int) * nseg);                   // hot segment ids, in order
-    float* hthr = (float*)take(sizeof(float) * nseg);            // significance threshold
-    float* hA = (float*)take(sizeof(float) * nseg);              // approx segment sums
-    int* hE = (int*)take(sizeof(int) * nseg);                    // predicted binade
-    Tf* htf = (Tf*)take(sizeof(Tf) * nseg);
-    int* ovi = (int*)take(sizeof(int) * (ov_stride > 0 ? ov_stride : 1));
-    float* ovv = (float*)take(sizeof(float) * (ov_stride > 0 ? ov_stride : 1));
-    float* ct = (float*)take(sizeof(float) * ccap);
-    int* ci = (int*)take(sizeof(int) * ccap);
-    float* cp = (float*)take(sizeof(float) * ccap);
-    int* so = (int*)take(sizeof(int) * ccap);                    // sorted order -> slot
-    unsigned long long* ck = (unsigned long long*)take(sizeof(unsigned long long) * ccap);
-    uint32_t* rhist = (uint32_t*)take(sizeof(uint32_t) * 256);
-    int* cseg = hot;  // candidate segment list reuses `hot` after the walk
-    __shared__ float red_f[32];
-    __shared__ int red_i[32];
-    __shared__ double red_d[32];
-    __shared__ int sh_misc[8];
-    __shared__ int sh_nhot, sh_ncand, sh_fb, sh_ncseg;
-    __shared__ float sh_sum, sh_r, sh_tau;
-
-    long long* ph = phase_cycles ? phase_cycles + (size_t)row * 10 : nullptr;
-    auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
-    stamp(0);
-
-    // ---- overrides
-    const int nov = ov_n ? ov_n[row] : 0;
-    for (int i = tid; i < nov; i += kRowThreads) {
-        ovi[i] = ov_idx[(size_t)row * ov_stride + i];
-        ovv[i] = ov_val[(size_t)row * ov_stride + i];
-    }
-    for (int g = tid; g < nseg; g += kRowThreads) segov[g] = 0;
-    __syncthreads();
-    for (int i = tid; i < nov; i += kRowThreads) segov[ovi[i] / SEG] = 1;
-    __syncthreads();
-
-    RowView<T> rv;
-    rv.L = logits + (size_t)row * V;
-    rv.V = V;
-    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
-    rv.segov = segov;
-    rv.ovi = ovi;
-    rv.ovv = ovv;
-    rv.nov = nov;
-    stamp(1);
-
-    // ---- A: streaming pass, segment maxima of the penalised logits
-    for (int g0 = warp; g0 < nseg; g0 += kRowWarps * U) {
-        uint4 r[U];
-        bool f[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int g = g0 + u * kRowWarps;
-            f[u] = (g < nseg) && rv.full(g, lane);
-            if (f[u]) r[u] = rv.raw(g, lane);
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int g = g0 + u * kRowWarps;
-            if (g < nseg) {
-                float m;
-                if (f[u] && !segov[g]) {
-                    m = vec_max<T>(r[u]);
-                } else {
-                    float v[EPL];
-                    rv.widen(g, lane, f[u], r[u], v);
-                    m = v[0];
-#pragma unroll
-                    for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
-                }
-                const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
-                if (lane == 0) segm[g] = fkey_inv(km);
-            }
-        }
-    }
-    __syncthreads();
-    float lm = -INFINITY;
-    for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
-    const float maxl = rblock_max(lm, red_f);
-    stamp(2);
-
-    RowResult out;
-    out.token = 0; out.greedy = 0; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
-    out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0; out.max_logit = maxl;
-    out.sum = 0.f; out.r = 0.f; out.renorm_sum = 0.f; out.inv_temp = 0.f; out.sum_inv = 0.f;
-    out.status = 0; out.pad_ = 0;
-
-    // ---- greedy: lowest index of the maximum penalised logit
-    if (prm.temperature < 1e-6f) {
-        int first = 0x7fffffff;
-        for (int g = tid; g < nseg; g += kRowThreads)
-            if (segm[g] == maxl) first = min(first, g);
-        first = rblock_min_int(first, red_i);
-        if (warp == 0) {
-            int best = 0x7fffffff;
-            if (first != 0x7fffffff) {
-                float v[EPL];
-                rv.load(first, lane, v);
-#pragma unroll
-                for (int e = EPL - 1; e >= 0; e--)
-                    if (v[e] == maxl) best = first * SEG + lane * EPL + e;
-            }
-            best = warp_min_int(best);
-            if (lane == 0) {
-                out.token = (best == 0x7fffffff) ? 0 : best;
-                out.greedy = 1;
-                res[row] = out;
-            }
-        }
-        return;
-    }
-
-    // ---- B: temperature, prefix maxima, hot segments
-    const float inv = __fdiv_rn(1.0f, prm.temperature);
-    const float M = __fmul_rn(maxl, inv);
-    for (int g = tid; g < nseg; g += kRowThreads) {
-        const float t = __fmul_rn(segm[g], inv);
-        segm[g] = t;
-        segk[g] = fkey(t);
-    }
-    // the row's uniform is drawn up front so every exit path advances the state
-    if (tid == 0) {
-        unsigned long long st = rng[row];
-        sh_r = xorshift_f32(&st);
-        rng[row] = st;
-    }
-    __syncthreads();
+    int* hot = (int*)region;                          // hot segment ids, in order
+    float* hthr = (float*)(region + 4 * (size_t)nseg);
+    float* hA = (float*)(region + 8 * (size_t)nseg);
+    int* hE = (int*)(region + 12 * (size_t)nseg);
+    Tf* htf = (Tf*)(region + 16 * (size_t)nseg);
     {
         const int per = (nseg + kRowThreads - 1) / kRowThreads;
         const int c0 = tid * per, c1 = min(c0 + per, nseg);
@@ -665,19 +557,19 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
             const float y = __shfl_up_sync(0xffffffffu, x, o);
             if (lane >= o) x = fmaxf(x, y);
         }
-        if (lane == 31) red_f[warp] = x;
+        if (lane == 31) sh->red_f[warp] = x;
         __syncthreads();
         if (warp == 0) {
-            float s = lane < kRowWarps ? red_f[lane] : -INFINITY;
+            float s = lane < kRowWarps ? sh->red_f[lane] : -INFINITY;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const float y = __shfl_up_sync(0xffffffffu, s, o);
                 if (lane >= o) s = fmaxf(s, y);
             }
-            if (lane < kRowWarps) red_f[lane] = s;
+            if (lane < kRowWarps) sh->red_f[lane] = s;
         }
         __syncthreads();
-        float before = (warp == 0) ? -INFINITY : red_f[warp - 1];
+        float before = (warp == 0) ? -INFINITY : sh->red_f[warp - 1];
         const float xin = __shfl_up_sync(0xffffffffu, x, 1);
         if (lane > 0) before = fmaxf(before, xin);
         int nh = 0;
@@ -688,24 +580,19 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
             run = fmaxf(run, segm[g]);
         }
         int tot;
-        int off = rblock_excl_scan(nh, red_i, &tot);
+        int off = rblock_excl_scan(nh, sh->red_i, &tot);
         run = before;
         for (int g = c0; g < c1; g++) {
             const float thr = __fsub_rn(run, kSigGap);
             if ((segm[g] >= thr) && (segm[g] > -INFINITY)) { hot[off] = g; hthr[off] = thr; off++; }
             run = fmaxf(run, segm[g]);
         }
-        if (tid == 0) sh_nhot = tot;
+        if (tid == 0) sh->nhot = tot;
     }
     __syncthreads();
-    const int nhot = sh_nhot;
-    stamp(3);
-
-    // ---- C: exact softmax denominator
-    // S1: significant elements per hot segment
-    int* hcnt = hE;              // reused: counts, then offsets (sparse path)
-    float* slist = (float*)htf;  // reused: index-ordered exponent arguments
-    const int list_cap = (int)((sizeof(Tf) * nseg) / sizeof(float));
+    const int nhot = sh->nhot;
+    // approximate sums of hot segments (binade prediction only, so CUDA's
+    // fast exponential is good enough here)
     for (int h0 = warp; h0 < nhot; h0 += kRowWarps * 4) {
         uint4 r[4];
         bool f[4];
@@ -722,11 +609,14 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
                 float v[EPL];
                 rv.widen(hot[h], lane, f[u], r[u], v);
                 const float thr = hthr[h];
-                int cnt = 0;
+                float s = 0.f;
 #pragma unroll
-                for (int e = 0; e < EPL; e++) cnt += (__fmul_rn(v[e], inv) >= thr);
-                cnt = __reduce_add_sync(0xffffffffu, (unsigned)cnt);
-                if (lane == 0) hcnt[h] = cnt;
+                for (int e = 0; e < EPL; e++) {
+                    const float t = __fmul_rn(v[e], inv);
+                    if (t >= thr) s += __expf(t - M);
+                }
+                s = warp_sum(s);
+                if (lane == 0) hA[h] = s;
             }
         }
     }
@@ -734,221 +624,205 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
     {
         const int per = (nhot + kRowThreads - 1) / kRowThreads;
         const int c0 = tid * per, c1 = min(c0 + per, nhot);
-        int cs = 0;
-        for (int h = c0; h < c1; h++) cs += hcnt[h];
-        int tot;
-        int off = rblock_excl_scan(cs, red_i, &tot);
-        for (int h = c0; h < c1; h++) { const int cc = hcnt[h]; hcnt[h] = off; off += cc; }
-        if (tid == 0) sh_misc[6] = tot;
-    }
-    __syncthreads();
-    const int nsig = sh_misc[6];
-    if (nsig <= list_cap) {
-        // S2: compact the significant elements' exponent arguments in index order
-        for (int h0 = warp; h0 < nhot; h0 += kRowWarps * 4) {
-            uint4 r[4];
-            bool f[4];
+        double cs = 0.0;
+        for (int h = c0; h < c1; h++) cs += (double)hA[h];
+        double x = cs;
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int h = h0 + u * kRowWarps;
-                f[u] = (h < nhot) && rv.full(hot[h], lane);
-                if (f[u]) r[u] = rv.raw(hot[h], lane);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int h = h0 + u * kRowWarps;
-                if (h < nhot) {
-                    float v[EPL];
-                    rv.widen(hot[h], lane, f[u], r[u], v);
-                    const float thr = hthr[h];
-                    int mine = 0;
-#pragma unroll
-                    for (int e = 0; e < EPL; e++) mine += (__fmul_rn(v[e], inv) >= thr);
-                    int incl = mine;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                        if (lane >= o) incl += y;
-                    }
-                    int pos = hcnt[h] + incl - mine;
-#pragma unroll
-                    for (int e = 0; e < EPL; e++) {
-                        const float t = __fmul_rn(v[e], inv);
-                        if (t >= thr) slist[pos++] = __fsub_rn(t, M);
-                    }
-                }
-            }
+        for (int o = 1; o < 32; o <<= 1) {
+            const double y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
         }
+        if (lane == 31) sh->red_d[warp] = x;
         __syncthreads();
         if (warp == 0) {
-            const float sres = walk_list(slist, nsig, 0.0f, fx);
-            if (lane == 0) { sh_sum = sres; sh_fb = -nsig; }
-        }
-    } else {
-        // ---- C1: approximate sums of hot segments (binade prediction only, so
-        //      CUDA's fast exponential is good enough here)
-        for (int h0 = warp; h0 < nhot; h0 += kRowWarps * 4) {
-            uint4 r[4];
-            bool f[4];
-    #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int h = h0 + u * kRowWarps;
-                f[u] = (h < nhot) && rv.full(hot[h], lane);
-                if (f[u]) r[u] = rv.raw(hot[h], lane);
-            }
-    #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int h = h0 + u * kRowWarps;
-                if (h < nhot) {
-                    float v[EPL];
-                    rv.widen(hot[h], lane, f[u], r[u], v);
-                    const float thr = hthr[h];
-                    float s = 0.f;
-    #pragma unroll
-                    for (int e = 0; e < EPL; e++) {
-                        const float t = __fmul_rn(v[e], inv);
-                        if (t >= thr) s += __expf(t - M);
-                    }
-                    s = warp_sum(s);
-                    if (lane == 0) hA[h] = s;
-                }
-            }
-        }
-        __syncthreads();
-        {
-            const int per = (nhot + kRowThreads - 1) / kRowThreads;
-            const int c0 = tid * per, c1 = min(c0 + per, nhot);
-            double cs = 0.0;
-            for (int h = c0; h < c1; h++) cs += (double)hA[h];
-            double x = cs;
-    #pragma unroll
+            double s = lane < kRowWarps ? sh->red_d[lane] : 0.0;
+#pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const double y = __shfl_up_sync(0xffffffffu, x, o);
-                if (lane >= o) x += y;
+                const double y = __shfl_up_sync(0xffffffffu, s, o);
+                if (lane >= o) s += y;
             }
-            if (lane == 31) red_d[warp] = x;
-            __syncthreads();
-            if (warp == 0) {
-                double s = lane < kRowWarps ? red_d[lane] : 0.0;
-    #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const double y = __shfl_up_sync(0xffffffffu, s, o);
-                    if (lane >= o) s += y;
-                }
-                if (lane < kRowWarps) red_d[lane] = s;
-            }
-            __syncthreads();
-            double run = ((warp == 0) ? 0.0 : red_d[warp - 1]) + (x - cs);
-            for (int h = c0; h < c1; h++) {
-                const double lo = run * (1.0 - (double)kDelta);
-                const double hi = (run + (double)hA[h]) * (1.0 + (double)kDelta);
-                int E = INT_MIN;
-                if (lo >= 2.3509887016445750e-38 && hi < 3.0e38) {  // at least 2^-125
-                    int e1, e2;
-                    frexp(lo, &e1);
-                    frexp(hi, &e2);
-                    if (e1 == e2) E = e1 - 1;
-                }
-                hE[h] = E;
-                run += (double)hA[h];
-            }
+            if (lane < kRowWarps) sh->red_d[lane] = s;
         }
         __syncthreads();
-        stamp(4);
-
-        // ---- C2: transfer functions of predictable hot segments
-        for (int h0 = warp; h0 < nhot; h0 += kRowWarps * 4) {
-            uint4 r[4];
-            bool f[4];
-    #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int h = h0 + u * kRowWarps;
-                f[u] = (h < nhot) && hE[h] != INT_MIN && rv.full(hot[h], lane);
-                if (f[u]) r[u] = rv.raw(hot[h], lane);
+        double run = ((warp == 0) ? 0.0 : sh->red_d[warp - 1]) + (x - cs);
+        for (int h = c0; h < c1; h++) {
+            const double lo = run * (1.0 - (double)kDelta);
+            const double hi = (run + (double)hA[h]) * (1.0 + (double)kDelta);
+            int E = INT_MIN;
+            if (lo >= 2.3509887016445750e-38 && hi < 3.0e38) {  // at least 2^-125
+                int e1, e2;
+                frexp(lo, &e1);
+                frexp(hi, &e2);
+                if (e1 == e2) E = e1 - 1;
             }
-    #pragma unroll 1
-            for (int u = 0; u < 4; u++) {
-                const int h = h0 + u * kRowWarps;
-                if (h < nhot && hE[h] != INT_MIN) {
-                    const int E = hE[h];
-                    float v[EPL];
-                    rv.widen(hot[h], lane, f[u], r[u], v);
-                    const float thr = hthr[h];
-                    Tf tf = tf_identity();
-    #pragma unroll
-                    for (int e = 0; e < EPL; e++) {
-                        const float t = __fmul_rn(v[e], inv);
-                        if (t >= thr) {
-                            const float d = __fsub_rn(t, M);
-                            tf = tf_compose(tf, tf_element(grid_term(d, expf(d), E, fx), E));
-                        }
-                    }
-                    // ordered reduction: lane 0 ends with the whole segment
-    #pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        Tf b;
-                        b.inc0 = __shfl_down_sync(0xffffffffu, tf.inc0, o);
-                        b.inc1 = __shfl_down_sync(0xffffffffu, tf.inc1, o);
-                        b.out = __shfl_down_sync(0xffffffffu, tf.out, o);
-                        b.ok = __shfl_down_sync(0xffffffffu, tf.ok, o);
-                        if ((lane & (2 * o - 1)) == 0) tf = tf_compose(tf, b);
-                    }
-                    if (lane == 0) htf[h] = tf;
-                }
-            }
-        }
-        __syncthreads();
-        stamp(5);
-
-        // ---- C3: the walk (warp 0) reproduces the sequential fp32 sum
-        if (warp == 0) {
-            float s = 0.0f;
-            int fb = 0;
-            int h = 0;
-            while (h < nhot) {
-                const int E = sum_binade(s);
-                const uint32_t S = sum_units(s, E);
-                const int hh = h + lane;
-                const bool inr = hh < nhot;
-                Tf f = tf_identity();
-                bool valid = false;
-                if (inr && hE[hh] == E) {
-                    f = htf[hh];
-                    valid = f.ok != 0;
-                }
-                const unsigned badm = __ballot_sync(0xffffffffu, inr && !valid);
-                const int first_bad = badm ? (__ffs(badm) - 1) : 32;
-                const Tf pre = warp_scan_tf(valid ? f : tf_identity());
-                const uint32_t inc = (S & 1u) ? pre.inc1 : pre.inc0;
-                const bool good = inr && lane < first_bad && (S + inc < kTwo24);
-                const unsigned gm = __ballot_sync(0xffffffffu, good);
-                const int nok = (gm == 0xffffffffu) ? 32 : (__ffs(~gm) - 1);
-                if (nok > 0) {
-                    const uint32_t add = __shfl_sync(0xffffffffu, inc, nok - 1);
-                    s = ldexpf((float)(S + add), E - 23);
-                    h += nok;
-                }
-                if (nok < 32 && h < nhot) {
-                    s = walk_segment<T>(rv, hot[h], hthr[h], inv, M, s, fx);
-                    fb++;
-                    h++;
-                }
-            }
-            if (lane == 0) { sh_sum = s; sh_fb = fb; }
+            hE[h] = E;
+            run += (double)hA[h];
         }
     }
     __syncthreads();
-    const float sum = sh_sum;
-    const float sum_inv = __fdiv_rn(1.0f, sum);
-    out.sum = sum;
-    out.sum_fallback = sh_fb;
-    out.max_logit = M;
-    out.inv_temp = inv;
-    out.sum_inv = sum_inv;
-    out.r = sh_r;
-    stamp(6);
+    // transfer functions of predictable hot segments
+    for (int h0 = warp; h0 < nhot; h0 += kRowWarps * 4) {
+        uint4 r[4];
+        bool f[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int h = h0 + u * kRowWarps;
+            f[u] = (h < nhot) && hE[h] != INT_MIN && rv.full(hot[h], lane);
+            if (f[u]) r[u] = rv.raw(hot[h], lane);
+        }
+#pragma unroll 1
+        for (int u = 0; u < 4; u++) {
+            const int h = h0 + u * kRowWarps;
+            if (h < nhot && hE[h] != INT_MIN) {
+                const int E = hE[h];
+                float v[EPL];
+                rv.widen(hot[h], lane, f[u], r[u], v);
+                const float thr = hthr[h];
+                Tf tf = tf_identity();
+#pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    const float t = __fmul_rn(v[e], inv);
+                    if (t >= thr) {
+                        const float d = __fsub_rn(t, M);
+                        tf = tf_compose(tf, tf_element(grid_term(d, expf(d), E, fx), E));
+                    }
+                }
+                // ordered reduction: lane 0 ends with the whole segment
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    Tf b;
+                    b.inc0 = __shfl_down_sync(0xffffffffu, tf.inc0, o);
+                    b.inc1 = __shfl_down_sync(0xffffffffu, tf.inc1, o);
+                    b.out = __shfl_down_sync(0xffffffffu, tf.out, o);
+                    b.ok = __shfl_down_sync(0xffffffffu, tf.ok, o);
+                    if ((lane & (2 * o - 1)) == 0) tf = tf_compose(tf, b);
+                }
+                if (lane == 0) htf[h] = tf;
+            }
+        }
+    }
+    __syncthreads();
+    // the walk (warp 0) reproduces the sequential fp32 sum
+    if (warp == 0) {
+        float s = 0.0f;
+        int fb = 0;
+        int h = 0;
+        while (h < nhot) {
+            const int E = sum_binade(s);
+            const uint32_t S = sum_units(s, E);
+            const int hh = h + lane;
+            const bool inr = hh < nhot;
+            Tf f = tf_identity();
+            bool valid = false;
+            if (inr && hE[hh] == E) {
+                f = htf[hh];
+                valid = f.ok != 0;
+            }
+            const unsigned badm = __ballot_sync(0xffffffffu, inr && !valid);
+            const int first_bad = badm ? (__ffs(badm) - 1) : 32;
+            const Tf pre = warp_scan_tf(valid ? f : tf_identity());
+            const uint32_t inc = (S & 1u) ? pre.inc1 : pre.inc0;
+            const bool good = inr && lane < first_bad && (S + inc < kTwo24);
+            const unsigned gm = __ballot_sync(0xffffffffu, good);
+            const int nok = (gm == 0xffffffffu) ? 32 : (__ffs(~gm) - 1);
+            if (nok > 0) {
+                const uint32_t add = __shfl_sync(0xffffffffu, inc, nok - 1);
+                s = ldexpf((float)(S + add), E - 23);
+                h += nok;
+            }
+            if (nok < 32 && h < nhot) {
+                s = walk_segment<T>(rv, hot[h], hthr[h], inv, M, s, fx);
+                fb++;
+                h++;
+            }
+        }
+        if (lane == 0) { sh->sum = s; sh->fb = fb; }
+    }
+}
 
-    // ---- D: candidates
+// Candidate arrays of one row.
+struct Cands {
+    float* ct;
+    int* ci;
+    float* cp;
+    int* so;
+    unsigned long long* ck;
+    uint32_t* rhist;
+    int cap;
+};
+
+// Where a row's results go.
+struct RowOut {
+    RowResult* res;
+    int* slow_list;
+    int* slow_count;
+    int* cand_index;
+    float* cand_prob;
+    int cand_cap;
+    int row;
+};
+
+// Ranks c candidates by (p desc, index asc) into cd.so, on order-preserving
+// integer keys: the same order as the float probabilities when they are
+// finite, and still a strict total order (so `so` stays a permutation) if a
+// row holds non-finite logits.  Block-wide.
+__device__ __noinline__ void rank_candidates(const Cands& cd, int c) {
+    const int tid = threadIdx.x;
+    if (c <= kRankSortMax) {
+        for (int i = tid; i < c; i += kRowThreads) {
+            const uint32_t ki = fkey(cd.cp[i]);
+            const int ii = cd.ci[i];
+            int rank = 0;
+            for (int j = 0; j < c; j++) {
+                const uint32_t kj = fkey(cd.cp[j]);
+                rank += (kj > ki) || (kj == ki && cd.ci[j] < ii);
+            }
+            cd.so[rank] = i;
+        }
+        __syncthreads();
+        return;
+    }
+    int npow = 1;
+    while (npow < c) npow <<= 1;
+    for (int i = tid; i < npow; i += kRowThreads)
+        cd.ck[i] = (i < c) ? (((unsigned long long)fkey(cd.cp[i]) << 32) | (unsigned long long)(uint32_t)i)
+                           : 0ull;
+    __syncthreads();
+    // ties in p must end in index order: sort keys carry the slot, so
+    // re-rank equal-p runs by index afterwards
+    rblock_sort_desc(cd.ck, npow);
+    for (int i = tid; i < c; i += kRowThreads) cd.so[i] = (int)(cd.ck[i] & 0xFFFFFFFFull);
+    __syncthreads();
+    if (tid == 0) {
+        int i = 0;
+        while (i < c) {
+            int j = i + 1;
+            while (j < c && fkey(cd.cp[cd.so[j]]) == fkey(cd.cp[cd.so[i]])) j++;
+            for (int a = i + 1; a < j; a++) {  // insertion sort of the run by index
+                const int x = cd.so[a];
+                int b = a - 1;
+                while (b >= i && cd.ci[cd.so[b]] > cd.ci[x]) { cd.so[b + 1] = cd.so[b]; b--; }
+                cd.so[b + 1] = x;
+            }
+            i = j;
+        }
+    }
+    __syncthreads();
+}
+
+// Candidates by segment maxima, re-read from L2, then min-p / top-p / draw
+// (rows the stash does not settle).  segm / segk hold the segment maxima of t
+// and their keys; cseg has room for nseg ids.
+template <typename T>
+__device__ __noinline__ void finish_by_segments(RowView<T> rv, int nseg, const float* segm,
+                                                const uint32_t* segk, int* cseg, Cands cd,
+                                                RowParams prm, float inv, float M, float sum_inv,
+                                                RowShared* sh, RowResult out, RowOut ro, ExpFix fx,
+                                                long long* ph) {
+    constexpr int EPL = RowView<T>::EPL;
+    constexpr int SEG = RowView<T>::SEG;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int V = rv.V;
     const bool use_topk = prm.top_k > 0 && prm.top_k < V;
     int m = use_topk ? prm.top_k : 64;
     int status = 0;
@@ -956,20 +830,20 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
     for (int attempt = 0;; attempt++) {
         if (m <= nseg) {
             if (warp == 0) {
-                const float tau = fkey_inv(warp_kth_largest(segk, nseg, m, rhist));
-                if (lane == 0) { sh_tau = tau; sh_ncand = 0; sh_ncseg = 0; }
+                const float tau = fkey_inv(warp_kth_largest(segk, nseg, m, cd.rhist));
+                if (lane == 0) { sh->tau = tau; sh->ncand = 0; sh->ncseg = 0; }
             }
         } else {
             const float tau = (m >= V) ? -INFINITY
-                                       : fkey_inv(block_kth_largest_row(rv, nseg, inv, m, rhist, sh_misc));
-            if (tid == 0) { sh_tau = tau; sh_ncand = 0; sh_ncseg = 0; }
+                                       : fkey_inv(block_kth_largest_row(rv, nseg, inv, m, cd.rhist, sh->misc));
+            if (tid == 0) { sh->tau = tau; sh->ncand = 0; sh->ncseg = 0; }
         }
         __syncthreads();
-        const float tau = sh_tau;
+        const float tau = sh->tau;
         for (int g = tid; g < nseg; g += kRowThreads)
-            if (segm[g] >= tau) cseg[atomicAdd(&sh_ncseg, 1)] = g;
+            if (segm[g] >= tau) cseg[atomicAdd(&sh->ncseg, 1)] = g;
         __syncthreads();
-        const int ncs = sh_ncseg;
+        const int ncs = sh->ncseg;
         for (int j0 = warp; j0 < ncs; j0 += kRowWarps * 4) {
             uint4 r[4];
             bool f[4];
@@ -991,69 +865,25 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
                         const int idx = g * SEG + lane * EPL + e;
                         const float t = __fmul_rn(v[e], inv);
                         if (idx < V && t >= tau) {
-                            const int pos = atomicAdd(&sh_ncand, 1);
-                            if (pos < ccap) { ct[pos] = t; ci[pos] = idx; }
+                            const int pos = atomicAdd(&sh->ncand, 1);
+                            if (pos < cd.cap) { cd.ct[pos] = t; cd.ci[pos] = idx; }
                         }
                     }
                 }
             }
         }
         __syncthreads();
-        c = sh_ncand;
-        if (c > ccap || (use_topk && c < prm.top_k) || c < 1) { status = 1; break; }
+        c = sh->ncand;
+        if (c > cd.cap || (use_topk && c < prm.top_k) || c < 1) { status = 1; break; }
         // exact probabilities (sampler.h:197-206) and the (p desc, index asc) order
         for (int i = tid; i < c; i += kRowThreads)
-            cp[i] = __fmul_rn(ref_expf(__fsub_rn(ct[i], M), fx), sum_inv);
+            cd.cp[i] = __fmul_rn(ref_expf(__fsub_rn(cd.ct[i], M), fx), sum_inv);
         __syncthreads();
-        if (c <= kRankSortMax) {
-            // rank on order-preserving integer keys: the same order as the
-            // float probabilities when they are finite, and still a strict
-            // total order (so `so` stays a permutation) if a row holds
-            // non-finite logits
-            for (int i = tid; i < c; i += kRowThreads) {
-                const uint32_t ki = fkey(cp[i]);
-                const int ii = ci[i];
-                int rank = 0;
-                for (int j = 0; j < c; j++) {
-                    const uint32_t kj = fkey(cp[j]);
-                    rank += (kj > ki) || (kj == ki && ci[j] < ii);
-                }
-                so[rank] = i;
-            }
-            __syncthreads();
-        } else {
-            int npow = 1;
-            while (npow < c) npow <<= 1;
-            for (int i = tid; i < npow; i += kRowThreads)
-                ck[i] = (i < c) ? (((unsigned long long)fkey(cp[i]) << 32) |
-                                   (unsigned long long)(uint32_t)i)
-                                : 0ull;
-            __syncthreads();
-            // ties in p must end in index order: sort keys carry the slot, so
-            // re-rank equal-p runs by index afterwards
-            rblock_sort_desc(ck, npow);
-            for (int i = tid; i < c; i += kRowThreads) so[i] = (int)(ck[i] & 0xFFFFFFFFull);
-            __syncthreads();
-            if (tid == 0) {
-                int i = 0;
-                while (i < c) {
-                    int j = i + 1;
-                    while (j < c && fkey(cp[so[j]]) == fkey(cp[so[i]])) j++;
-                    for (int a = i + 1; a < j; a++) {  // insertion sort of the run by index
-                        const int x = so[a];
-                        int b = a - 1;
-                        while (b >= i && ci[so[b]] > ci[x]) { so[b + 1] = so[b]; b--; }
-                        so[b + 1] = x;
-                    }
-                    i = j;
-                }
-            }
-            __syncthreads();
-        }
+        rank_candidates(cd, c);
         if (use_topk) break;
         // full-sort mode: is the needed prefix inside the certain part?
         if (tid == 0) {
-            auto P = [&](int i) { return cp[so[i]]; };
+            auto P = [&](int i) { return cd.cp[cd.so[i]]; };
             const float pmin = P(c - 1);
             int ncert = 0;
             if (c == V) ncert = c;
@@ -1078,15 +908,15 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
                 else if (n > ncert) ok = false;  // the cut could lie beyond the certain prefix
             }
             if (ok && n > ncert) ok = false;
-            sh_misc[4] = ok ? n : -1;
+            sh->misc[4] = ok ? n : -1;
         }
         __syncthreads();
-        if (sh_misc[4] >= 0) break;
-        if (m >= ccap / 2 || m >= V) { status = 2; break; }
-        m = min(m * 8, ccap / 2);
+        if (sh->misc[4] >= 0) break;
+        if (m >= cd.cap / 2 || m >= V) { status = 2; break; }
+        m = min(m * 8, cd.cap / 2);
         __syncthreads();
     }
-    stamp(7);
+    if (ph && tid == 0) ph[7] = clock64();
 
     if (status != 0) {
         // the fast kernel cannot hold this row's candidates; the exact pass
@@ -1095,19 +925,19 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
             out.status = status;
             out.token = -1;
             if (use_topk && !(prm.flags & QS_FLAG_INDEX_TIES)) {
-                const int slot = atomicAdd(slow_count, 1);
-                slow_list[slot] = row;
+                const int slot = atomicAdd(ro.slow_count, 1);
+                ro.slow_list[slot] = ro.row;
                 out.exact_ties = 1;
             }
-            res[row] = out;
+            ro.res[ro.row] = out;
         }
         return;
     }
 
-    // ---- E: min-p, top-p, renormalise, draw (serial, thread 0)
+    // min-p, top-p, renormalise, draw (serial, thread 0)
     if (tid == 0) {
-        auto P = [&](int i) { return cp[so[i]]; };
-        auto I = [&](int i) { return ci[so[i]]; };
+        auto P = [&](int i) { return cd.cp[cd.so[i]]; };
+        auto I = [&](int i) { return cd.ci[cd.so[i]]; };
         int n = use_topk ? prm.top_k : (c == V ? V : c);
         out.n_topk = use_topk ? prm.top_k : V;
         if (prm.minp > 0.0f && n > 0) {
@@ -1133,7 +963,7 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
         for (int i = 0; i < n; i++) s2 = __fadd_rn(s2, P(i));
         const float inv2 = __fdiv_rn(1.0f, s2);
         out.renorm_sum = s2;
-        const float r = sh_r;
+        const float r = sh->r;
         float cum = 0.f;
         int pos = n - 1;
         for (int i = 0; i < n; i++) {
@@ -1157,21 +987,446 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
                 sensitive = (eq_all > grp) || uncertain;
             }
             if (sensitive && !(prm.flags & QS_FLAG_INDEX_TIES)) {
-                const int slot = atomicAdd(slow_count, 1);
-                slow_list[slot] = row;
+                const int slot = atomicAdd(ro.slow_count, 1);
+                ro.slow_list[slot] = ro.row;
                 out.exact_ties = 1;
             }
         }
-        res[row] = out;
-        if (ph) { ph[8] = clock64(); ph[9] = nhot | ((long long)c << 20) | ((long long)sh_fb << 40); }
-        if (cand_index_out) {
-            const int lim = min(use_topk ? prm.top_k : c, cand_cap);
+        ro.res[ro.row] = out;
+        if (ph) { ph[8] = clock64(); ph[9] = (long long)c << 20; }
+        if (ro.cand_index) {
+            const int lim = min(use_topk ? prm.top_k : c, ro.cand_cap);
             for (int i = 0; i < lim; i++) {
-                cand_index_out[(size_t)row * cand_cap + i] = I(i);
-                cand_prob_out[(size_t)row * cand_cap + i] = i < n ? __fmul_rn(P(i), inv2) : P(i);
+                ro.cand_index[(size_t)ro.row * ro.cand_cap + i] = I(i);
+                ro.cand_prob[(size_t)ro.row * ro.cand_cap + i] = i < n ? __fmul_rn(P(i), inv2) : P(i);
             }
         }
     }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
+row_kernel(const T* __restrict__ logits, int V, RowParams prm,
+           const int* __restrict__ ov_n, const int* __restrict__ ov_idx,
+           const float* __restrict__ ov_val, int ov_stride,
+           unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
+           int* __restrict__ slow_list, int* __restrict__ slow_count,
+           int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
+           ExpFix fx, int ccap, int scap, long long* __restrict__ phase_cycles) {
+    constexpr int EPL = Elem<T>::kPerLane;
+    constexpr int SEG = 32 * EPL;
+    constexpr int U = kRowRound / kRowWarps;  // segments in flight per warp in the streaming pass
+    const int row = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const RowSmem L(V, SEG, ov_stride, ccap, scap);
+    const int nseg = L.nseg;
+
+    // ---- shared memory carve-up
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* segm = (float*)(smem + L.segm);            // segment maxima (l, then t)
+    uint32_t* segk = (uint32_t*)(smem + L.segk);      // order keys of segm (t)
+    unsigned char* segov = smem + L.segov;
+    int* ovi = (int*)(smem + L.ovi);
+    float* ovv = (float*)(smem + L.ovv);
+    uint32_t* pubr = (uint32_t*)(smem + L.pubr);      // per streaming round: max key seen
+    unsigned char* region = smem + L.region;          // stash, or the dense method's tables
+    float* st_t = (float*)region;
+    int* st_i = (int*)(region + 4 * (size_t)scap);
+    float* st_e = (float*)(region + 8 * (size_t)scap);   // expf(t - max), the reference's term
+    float* slist = (float*)(region + 12 * (size_t)scap); // terms in index order
+    int* sstart = (int*)(region + 16 * (size_t)scap);
+    int* scnt = sstart + nseg;
+    const Cands cd{(float*)(smem + L.ct), (int*)(smem + L.ci), (float*)(smem + L.cp),
+                   (int*)(smem + L.so), (unsigned long long*)(smem + L.ck),
+                   (uint32_t*)(smem + L.rhist), ccap};
+    __shared__ RowShared sh;
+    const RowOut ro{res, slow_list, slow_count, cand_index_out, cand_prob_out, cand_cap, row};
+
+    long long* ph = phase_cycles ? phase_cycles + (size_t)row * 10 : nullptr;
+    auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
+    stamp(0);
+
+    const bool greedy = prm.temperature < 1e-6f;
+    const float inv = greedy ? 1.0f : __fdiv_rn(1.0f, prm.temperature);
+
+    // ---- overrides, tables
+    const int nov = ov_n ? ov_n[row] : 0;
+    for (int i = tid; i < nov; i += kRowThreads) {
+        ovi[i] = ov_idx[(size_t)row * ov_stride + i];
+        ovv[i] = ov_val[(size_t)row * ov_stride + i];
+    }
+    for (int g = tid; g < nseg; g += kRowThreads) { segov[g] = 0; scnt[g] = 0; }
+    for (int j = tid; j < L.nrounds; j += kRowThreads) pubr[j] = fkey(-INFINITY);
+    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); }
+    __syncthreads();
+    for (int i = tid; i < nov; i += kRowThreads) segov[ovi[i] / SEG] = 1;
+    __syncthreads();
+
+    RowView<T> rv;
+    rv.L = logits + (size_t)row * V;
+    rv.V = V;
+    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
+    rv.segov = segov;
+    rv.ovi = ovi;
+    rv.ovv = ovv;
+    rv.nov = nov;
+    stamp(1);
+
+    // ---- A: streaming pass.  Segment maxima of the penalised logits, and a
+    // stash of every element that may be significant for the softmax sum:
+    // t >= lb - 17.5 where lb is a lower bound of the maximum t over the
+    // segments before it (exact for the first round; afterwards the maxima
+    // published for earlier rounds).
+    float lb = -INFINITY;
+    float lbmax = -INFINITY;  // largest lb used: the stash holds every t >= lbmax - 17.5
+    uint4 r[U];  // this round's vectors; the next round's are requested as soon as
+                 // this round's maxima are taken (the stash re-reads from L2)
+    auto request = [&](int jj) {
+        const int gb = jj * kRowRound + warp;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int g = gb + u * kRowWarps;
+            if ((g < nseg) && rv.full(g, lane)) r[u] = rv.raw(g, lane);
+            else r[u] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    request(0);
+    for (int j = 0; j < L.nrounds; j++) {
+        const int g0 = j * kRowRound + warp;
+        unsigned slow = 0;  // segments that are partial or hold overrides (warp-uniform)
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int g = g0 + u * kRowWarps;
+            if (g < nseg) {
+                if (rv.aligned && (g + 1) * SEG <= V && !segov[g]) {
+                    const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(vec_max<T>(r[u])));
+                    if (lane == 0) segm[g] = fkey_inv(km);
+                } else {
+                    slow |= 1u << u;
+                }
+            }
+        }
+        if (j + 1 < L.nrounds) request(j + 1);
+        while (slow) {
+            const int u = __ffs(slow) - 1;
+            slow &= slow - 1;
+            const int g = g0 + u * kRowWarps;
+            float v[EPL];
+            rv.load(g, lane, v);
+            float m = v[0];
+#pragma unroll
+            for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
+            const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
+            if (lane == 0) segm[g] = fkey_inv(km);
+        }
+        __syncwarp();
+        if (greedy) continue;
+        // stash thresholds: round 0 per segment from exact prefix maxima
+        // (lane i holds those of its kRowRound / 32 segments), later rounds one
+        float pa = -INFINITY, pb = -INFINITY, thr_all = -INFINITY;
+        if (j == 0) {
+            __syncthreads();
+            constexpr int SPL = kRowRound / 32;  // segments per lane (1 or 2)
+            const int a = SPL * lane, b = SPL * lane + 1;
+            const float ta = a < nseg ? __fmul_rn(segm[a], inv) : -INFINITY;
+            const float tb = (SPL == 2 && b < nseg) ? __fmul_rn(segm[b], inv) : -INFINITY;
+            float x = fmaxf(ta, tb);
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x = fmaxf(x, y);
+            }
+            pa = __shfl_up_sync(0xffffffffu, x, 1);
+            if (lane == 0) pa = -INFINITY;
+            pb = fmaxf(pa, ta);
+            lb = __shfl_sync(0xffffffffu, x, 31);  // maximum of the whole first round
+        } else {
+            lb = fmaxf(lb, fkey_inv(*(volatile uint32_t*)&pubr[j - 1]));
+            lbmax = fmaxf(lbmax, lb);
+            thr_all = __fsub_rn(lb, kSigGap);
+        }
+        auto seg_thr = [&](int g) {  // warp-uniform g
+            if (j != 0) return thr_all;
+            constexpr int SPL = kRowRound / 32;
+            const int src = (g % kRowRound) / SPL;
+            const float qa = __shfl_sync(0xffffffffu, pa, src);
+            const float qb = __shfl_sync(0xffffffffu, pb, src);
+            return __fsub_rn((SPL == 2 && (g & 1)) ? qb : qa, kSigGap);
+        };
+        float rmax = -INFINITY;
+        unsigned want = 0;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int g = g0 + u * kRowWarps;
+            const float th = seg_thr(g);
+            if (g >= nseg) continue;
+            if (j == 0) lbmax = fmaxf(lbmax, __fadd_rn(th, kSigGap));
+            const float tmax = __fmul_rn(segm[g], inv);
+            rmax = fmaxf(rmax, tmax);
+            if (tmax >= th) want |= 1u << u;
+        }
+        while (want) {
+            const int u = __ffs(want) - 1;
+            want &= want - 1;
+            const int g = g0 + u * kRowWarps;
+            const float th = seg_thr(g);
+            float v[EPL];
+            rv.load(g, lane, v);
+            unsigned keep = 0;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                v[e] = __fmul_rn(v[e], inv);
+                const bool k = (g * SEG + lane * EPL + e < V) && v[e] >= th;
+                keep |= (k ? 1u : 0u) << e;
+            }
+            const int cnt = __popc(keep);
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const int tot = __shfl_sync(0xffffffffu, incl, 31);
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&sh.nst, tot);
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (base + tot <= scap) {
+                if (lane == 0) { sstart[g] = base; scnt[g] = tot; }
+                int pos = base + incl - cnt;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    if ((keep >> e) & 1u) {
+                        st_t[pos] = v[e];
+                        st_i[pos] = g * SEG + lane * EPL + e;
+                        pos++;
+                    }
+                }
+            } else if (lane == 0) {
+                sh.ovf = 1;
+            }
+        }
+        if (lane == 0) atomicMax(&pubr[j], fkey(rmax));
+    }
+    if (!greedy && lane == 0) atomicMax(&sh.maxlb, fkey(lbmax));
+    __syncthreads();
+    float lm = -INFINITY;
+    for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
+    const float maxl = rblock_max(lm, sh.red_f);
+    stamp(2);
+
+    RowResult out;
+    out.token = 0; out.greedy = 0; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
+    out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0; out.max_logit = maxl;
+    out.sum = 0.f; out.r = 0.f; out.renorm_sum = 0.f; out.inv_temp = 0.f; out.sum_inv = 0.f;
+    out.status = 0; out.pad_ = 0;
+
+    // ---- greedy: lowest index of the maximum penalised logit
+    if (greedy) {
+        int first = 0x7fffffff;
+        for (int g = tid; g < nseg; g += kRowThreads)
+            if (segm[g] == maxl) first = min(first, g);
+        first = rblock_min_int(first, sh.red_i);
+        if (warp == 0) {
+            int best = 0x7fffffff;
+            if (first != 0x7fffffff) {
+                float v[EPL];
+                rv.load(first, lane, v);
+#pragma unroll
+                for (int e = EPL - 1; e >= 0; e--)
+                    if (v[e] == maxl) best = first * SEG + lane * EPL + e;
+            }
+            best = warp_min_int(best);
+            if (lane == 0) {
+                out.token = (best == 0x7fffffff) ? 0 : best;
+                out.greedy = 1;
+                res[row] = out;
+            }
+        }
+        return;
+    }
+
+    // ---- B: temperature on the segment maxima; the row's uniform
+    const float M = __fmul_rn(maxl, inv);
+    for (int g = tid; g < nseg; g += kRowThreads) {
+        const float t = __fmul_rn(segm[g], inv);
+        segm[g] = t;
+        segk[g] = fkey(t);
+    }
+    // the row's uniform is drawn up front so every exit path advances the state
+    if (tid == 0) {
+        unsigned long long s = rng[row];
+        sh.r = xorshift_f32(&s);
+        rng[row] = s;
+        sh.done = 0;
+        sh.ncand = 0;
+        sh.nknown = 0;
+    }
+    __syncthreads();
+    const bool dense = sh.ovf != 0;
+    const int nst = sh.nst;
+    const float theta = __fsub_rn(fkey_inv(sh.maxlb), kSigGap);
+    stamp(3);
+
+    // ---- C: exact softmax denominator (sampler.h:195-201)
+    if (!dense) {
+        // the stashed terms, then the stash in index order, added in order
+        for (int i = tid; i < nst; i += kRowThreads) st_e[i] = ref_expf(__fsub_rn(st_t[i], M), fx);
+        {
+            const int per = (nseg + kRowThreads - 1) / kRowThreads;
+            const int c0 = tid * per, c1 = min(c0 + per, nseg);
+            int cs = 0;
+            for (int g = c0; g < c1; g++) cs += scnt[g];
+            int tot;
+            int off = rblock_excl_scan(cs, sh.red_i, &tot);
+            for (int g = c0; g < c1; g++) { const int cc = scnt[g]; scnt[g] = off; off += cc; }
+        }
+        __syncthreads();
+        stamp(4);
+        for (int i = tid; i < nst; i += kRowThreads) {
+            const int g = st_i[i] / SEG;
+            slist[scnt[g] + i - sstart[g]] = st_e[i];
+        }
+        __syncthreads();
+        stamp(5);
+        if (tid == 0) { sh.sum = serial_sum(slist, nst, 0.0f); sh.fb = -nst; }
+    } else {
+        dense_sum<T>(rv, nseg, segm, inv, M, region, &sh, fx);
+    }
+    __syncthreads();
+    const float sum = sh.sum;
+    const float sum_inv = __fdiv_rn(1.0f, sum);
+    out.sum = sum;
+    out.sum_fallback = sh.fb;
+    out.max_logit = M;
+    out.inv_temp = inv;
+    out.sum_inv = sum_inv;
+    out.r = sh.r;
+    stamp(6);
+
+    // ---- D, E from the stash.  It holds every element with t >= theta, so
+    // the reference's sorted list begins with these elements: entirely when at
+    // least K of them exist, else up to the first position whose probability
+    // an element outside the stash could equal.  The row is finished here when
+    // everything the draw reads lies in that known prefix.
+    if (!dense) {
+        const bool use_topk = prm.top_k > 0 && prm.top_k < V;
+        const int K = use_topk ? prm.top_k : V;
+        uint32_t* keys = reinterpret_cast<uint32_t*>(slist);  // the ordered terms are no longer needed
+        for (int i = tid; i < nst; i += kRowThreads)
+            if (st_t[i] >= theta) keys[atomicAdd(&sh.nknown, 1)] = fkey(st_t[i]);
+        __syncthreads();
+        const int nknown = sh.nknown;
+        const bool complete = nknown >= K;
+        if (complete && warp == 0) {
+            const float tau = fkey_inv(warp_kth_largest(keys, nknown, K, cd.rhist));
+            if (lane == 0) sh.tau = tau;
+        }
+        if (!complete && tid == 0) sh.tau = theta;
+        __syncthreads();
+        const float tau = sh.tau;
+        for (int i = tid; i < nst; i += kRowThreads) {
+            const float t = st_t[i];
+            if (t >= theta && t >= tau) {
+                const int pos = atomicAdd(&sh.ncand, 1);
+                if (pos < ccap) { cd.ci[pos] = st_i[i]; cd.cp[pos] = __fmul_rn(st_e[i], sum_inv); }
+            }
+        }
+        __syncthreads();
+        const int c = sh.ncand;
+        if (c >= 1 && c <= kRankSortMax && c <= ccap) {
+            rank_candidates(cd, c);
+            stamp(7);
+            if (tid == 0) {
+                auto P = [&](int i) { return cd.cp[cd.so[i]]; };
+                auto I = [&](int i) { return cd.ci[cd.so[i]]; };
+                // probabilities an element outside the stash can reach: at most p(theta)
+                const float ptheta = complete ? 0.0f : __fmul_rn(exact_exp(__fsub_rn(theta, M), fx), sum_inv);
+                int cert = c;  // leading positions whose element and probability are certain
+                if (!complete) { cert = 0; while (cert < c && P(cert) > ptheta) cert++; }
+                bool ok = cert >= 1;
+                int n = K;
+                if (ok && prm.minp > 0.0f) {
+                    float pmax = P(0);
+                    if (complete) for (int i = 1; i < K; i++) if (P(i) > pmax) pmax = P(i);
+                    const float thrp = __fmul_rn(prm.minp, pmax);
+                    if (complete || thrp > ptheta) {
+                        int kept = 0;
+                        const int lim = complete ? K : cert;
+                        while (kept < lim && P(kept) >= thrp) kept++;
+                        n = kept > 0 ? kept : 1;
+                    } else {
+                        ok = false;  // elements outside the stash could pass min-p
+                    }
+                }
+                const int n_minp = n;
+                if (ok && prm.topp < 1.0f && prm.topp > 0.0f) {
+                    float cum = 0.f;
+                    int cut = 0;
+                    const int lim = n < cert ? n : cert;
+                    for (int i = 0; i < lim; i++) {
+                        cum = __fadd_rn(cum, P(i));
+                        if (cum >= prm.topp) { cut = i + 1; break; }
+                    }
+                    if (cut > 0) n = cut;
+                }
+                if (ok && n > cert) ok = false;
+                if (ok && cand_index_out && min(K, cand_cap) > cert) ok = false;
+                if (ok) {
+                    out.n_topk = K;
+                    out.n_minp = n_minp;
+                    out.n_final = n;
+                    float s2 = 0.f;
+                    for (int i = 0; i < n; i++) s2 = __fadd_rn(s2, P(i));
+                    const float inv2 = __fdiv_rn(1.0f, s2);
+                    out.renorm_sum = s2;
+                    const float r = sh.r;
+                    float cum = 0.f;
+                    int pos = n - 1;
+                    for (int i = 0; i < n; i++) {
+                        cum = __fadd_rn(cum, __fmul_rn(P(i), inv2));
+                        if (r < cum) { pos = i; break; }
+                    }
+                    out.draw_pos = pos;
+                    out.token = I(pos);
+                    if (use_topk) {
+                        // does the drawn identity depend on the reference's tie arrangement?
+                        const float pv = P(pos);
+                        int grp = 0;
+                        for (int i = 0; i < cert && i < K; i++) grp += (P(i) == pv);
+                        bool sensitive = grp > 1;
+                        if (complete && !sensitive) {
+                            const float pk = P(K - 1);
+                            if (pv == pk) {
+                                int eq_all = 0;
+                                for (int i = 0; i < c; i++) eq_all += (P(i) == pk);
+                                const bool uncertain = (c < V) && (P(c - 1) == pk);
+                                sensitive = (eq_all > grp) || uncertain;
+                            }
+                        }
+                        if (sensitive && !(prm.flags & QS_FLAG_INDEX_TIES)) {
+                            const int slot = atomicAdd(slow_count, 1);
+                            slow_list[slot] = row;
+                            out.exact_ties = 1;
+                        }
+                    }
+                    res[row] = out;
+                    if (ph) { ph[8] = clock64(); ph[9] = (long long)nst | ((long long)c << 20) | (1ll << 40); }
+                    if (cand_index_out) {
+                        const int lim = min(K, cand_cap);
+                        for (int i = 0; i < lim; i++) {
+                            cand_index_out[(size_t)row * cand_cap + i] = I(i);
+                            cand_prob_out[(size_t)row * cand_cap + i] = i < n ? __fmul_rn(P(i), inv2) : P(i);
+                        }
+                    }
+                    sh.done = 1;
+                }
+            }
+            __syncthreads();
+        }
+        if (sh.done) return;
+    }
+    finish_by_segments<T>(rv, nseg, segm, segk, reinterpret_cast<int*>(region), cd, prm, inv, M,
+                          sum_inv, &sh, out, ro, fx, ph);
 }
 
 // ------------------------------------------------------------- launchers
@@ -1185,18 +1440,8 @@ int row_kernel_ccap(int top_k, int V) {
 }
 
 size_t row_kernel_smem(int V, int dtype_bytes, int ov_stride, int ccap) {
-    const int SEG = 32 * (16 / dtype_bytes);
-    const size_t nseg = (size_t)(V + SEG - 1) / SEG;
-    auto r16 = [](size_t b) { return (b + 15) & ~(size_t)15; };
-    size_t s = 0;
-    s += r16(4 * nseg) * 2;              // segm, segk
-    s += r16(nseg);                      // segov
-    s += r16(4 * nseg) * 4;              // hot, hthr, hA, hE
-    s += r16(sizeof(Tf) * nseg);
-    s += r16(4 * (size_t)(ov_stride > 0 ? ov_stride : 1)) * 2;
-    s += r16(4 * (size_t)ccap) * 4 + r16(8 * (size_t)ccap);
-    s += r16(4 * 256);
-    return s;
+    const RowSmem L(V, 32 * (16 / dtype_bytes), ov_stride, ccap, kStashCap);
+    return L.total;
 }
 
 template <typename T>
@@ -1212,7 +1457,8 @@ cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, cons
     if (err != cudaSuccess) return err;
     row_kernel<T><<<B, kRowThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val, ov_stride,
                                                     rng, res, slow_list, slow_count, cand_index,
-                                                    cand_prob, cand_cap, fx, ccap, phase_cycles);
+                                                    cand_prob, cand_cap, fx, ccap, kStashCap,
+                                                    phase_cycles);
     return cudaGetLastError();
 }
 
