@@ -12,7 +12,8 @@
 // logits t rather than the probabilities p = g(t): g is monotone, so
 // "p <= P" is "t <= t_hi" and "p >= P" is "t >= t_lo" for the interval
 // [t_lo, t_hi] of scaled logits whose probability equals the pivot's, which
-// is found exactly per round with a few evaluations of g.  Scans:
+// is found exactly per round by one warp evaluating g at 32 keys at once.
+// Scans:
 //
 //   L = positions whose value <= pivot (where the left scan stops), ascending
 //   R = positions whose value >= pivot (where the right scan stops), descending
@@ -20,54 +21,43 @@
 //   inclusive ranks a(q) = #L in [lo, q], b(q) = #R in [q, hi] is swapped as
 //   an L iff b(q) >= a(q) and as an R iff a(q) >= b(q)
 //
-// and the scans' final i / j follow from the last swap (see partition_round).
-// Then the reference's min-p / top-p / renormalise / draw run on the exact
+// and the scans' final i / j follow from the last swap (see final_ij).
+//
+// One slow row is handled by a cluster of kTieCluster CTAs on as many SMs:
+// while the active range is large each CTA partitions a contiguous slice of
+// it in global memory (L2), and the CTAs exchange their L / R / swap counts
+// through distributed shared memory between cluster barriers.  Once the range
+// fits in shared memory, the cluster's first CTA finishes the rounds there,
+// then runs the reference's min-p / top-p / renormalise / draw on the exact
 // order, with the uniform the row kernel already drew.
+#include <cooperative_groups.h>
+
 #include "qs_common.cuh"
 
 namespace qs {
 
-constexpr int kTieThreads = 1024;
+namespace cg = cooperative_groups;
+
+constexpr int kTieCluster = 8;           // CTAs (SMs) per slow row
+constexpr int kTieThreads = 256;
 constexpr int kTieWarps = kTieThreads / 32;
-constexpr int kTieSmemRange = 4096;  // active ranges up to this size continue in shared memory
+constexpr int kTieSmemRange = 2048;      // active ranges up to this size continue in shared memory
+constexpr int kTieSortCap = kCandCap / 2; // top-k limit of the API: the sorted prefix fits
+#ifndef QS_TIE_UN
+#define QS_TIE_UN 16
+#endif
 
-__device__ __forceinline__ int tie_excl_scan(int v, int* red, int* total) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    __syncthreads();
-    if (lane == 31) red[w] = x;
-    __syncthreads();
-    if (w == 0) {
-        int s = lane < kTieWarps ? red[lane] : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            int y = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += y;
-        }
-        if (lane < kTieWarps) red[lane] = s;
-    }
-    __syncthreads();
-    int before = (w == 0) ? 0 : red[w - 1];
-    *total = red[kTieWarps - 1];
-    return before + x - v;
-}
-
-// Exclusive block scan of two ints at once (one value per warp, held in lane
-// 0); returns both offsets and totals.
-__device__ __forceinline__ void tie_excl_scan2(int a, int b, int* red, int* oa, int* ob, int* ta,
+// Exclusive scan over the CTA's warps of two per-warp counts (valid in lane
+// 0 of each warp); returns this warp's offsets and the CTA totals.
+__device__ __forceinline__ void tie_warp_scan2(int a, int b, int* red, int* oa, int* ob, int* ta,
                                                int* tb) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     __syncthreads();
     if (lane == 0) { red[w] = a; red[32 + w] = b; }
     __syncthreads();
     if (w == 0) {
-        int x = lane < kTieWarps ? red[lane] : 0;
-        int y = lane < kTieWarps ? red[32 + lane] : 0;
+        const int x = lane < kTieWarps ? red[lane] : 0;
+        const int y = lane < kTieWarps ? red[32 + lane] : 0;
         int ix = x, iy = y;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -86,7 +76,7 @@ __device__ __forceinline__ void tie_excl_scan2(int a, int b, int* red, int* oa, 
     *tb = red[129];
 }
 
-__device__ __forceinline__ int tie_sum(int v, int* red) {
+__device__ __forceinline__ int tie_cta_sum(int v, int* red) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -99,111 +89,157 @@ __device__ __forceinline__ int tie_sum(int v, int* red) {
     return r;
 }
 
-__device__ __forceinline__ uint32_t pbits(unsigned long long a) { return (uint32_t)(a >> 32); }
+// Array accessors: keys (order keys of t) and element indices in separate
+// arrays.  Global scratch is shared by the cluster's CTAs on different SMs,
+// so it bypasses L1 (ld/st .cg); shared memory is plain.
+struct GlobalArr {
+    uint32_t* k;
+    int* idx;
+    __device__ __forceinline__ uint32_t key(int q) const { return __ldcg(k + q); }
+    __device__ __forceinline__ int index(int q) const { return __ldcg(idx + q); }
+    __device__ __forceinline__ void put(int q, uint32_t kv, int iv) const { __stcg(k + q, kv); __stcg(idx + q, iv); }
+};
+struct SharedArr {
+    uint32_t* k;  // indexed by position - offset
+    int* idx;
+    __device__ __forceinline__ uint32_t key(int q) const { return k[q]; }
+    __device__ __forceinline__ int index(int q) const { return idx[q]; }
+    __device__ __forceinline__ void put(int q, uint32_t kv, int iv) const { k[q] = kv; idx[q] = iv; }
+};
+struct GlobalPos {
+    int* p;
+    __device__ __forceinline__ int ld(int i) const { return __ldcg(p + i); }
+    __device__ __forceinline__ void st(int i, int v) const { __stcg(p + i, v); }
+};
+struct SharedPos {
+    int* p;
+    __device__ __forceinline__ int ld(int i) const { return p[i]; }
+    __device__ __forceinline__ void st(int i, int v) const { p[i] = v; }
+};
 
-// One round of the reference's partition loop on A[lo..hi]; the pivot's
-// probability is that of every key in [klo, khi].  Each warp owns a
-// contiguous chunk of the range and walks it 32 entries at a time (coalesced
-// loads); inclusive ranks come from ballots, chunk offsets from a block scan.
-// Returns the scans' final (i, j) in *oi / *oj (valid in every thread).
-__device__ void partition_round(unsigned long long* A, int lo, int hi, uint32_t klo, uint32_t khi,
-                                int* posL, int* posR, int* red, int* sh, int* oi, int* oj) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n = hi - lo + 1;
-    const int per = (n + kTieWarps - 1) / kTieWarps;
-    const int c0 = lo + warp * per;
-    const int c1 = min(c0 + per, hi + 1);
-    const unsigned lt = (1u << lane) - 1u;
-    constexpr int UN = 8;  // loads in flight per lane
-    int cl = 0, cr = 0;
+// Stop tests of a round.  Keys that are order keys of t compare with the
+// interval [klo, khi] of keys whose probability equals the pivot's; keys that
+// are the probabilities' bits compare as the reference compares them.
+struct KeyPivot {
+    uint32_t klo, khi;
+    __device__ __forceinline__ bool le(uint32_t v) const { return v <= khi; }  // left scan stops
+    __device__ __forceinline__ bool ge(uint32_t v) const { return v >= klo; }  // right scan stops
+};
+struct ProbPivot {
+    float P;
+    __device__ __forceinline__ bool le(uint32_t v) const { return !(__uint_as_float(v) > P); }
+    __device__ __forceinline__ bool ge(uint32_t v) const { return !(__uint_as_float(v) < P); }
+};
+
+// Counts of L and R stops in [c0, c1), by one warp, 256 positions per step.
+template <class Arr, class Pred>
+__device__ __forceinline__ void count_stops(const Arr& A, int c0, int c1, const Pred& pv, int* cl,
+                                            int* cr) {
+    const int lane = threadIdx.x & 31;
+    constexpr int UN = QS_TIE_UN;
+    int l = 0, r = 0;
     for (int q0 = c0; q0 < c1; q0 += 32 * UN) {
         uint32_t v[UN];
 #pragma unroll
         for (int u = 0; u < UN; u++) {
             const int q = q0 + u * 32 + lane;
-            v[u] = (q < c1) ? pbits(A[q]) : 0u;
+            v[u] = (q < c1) ? A.key(q) : 0u;
         }
 #pragma unroll
         for (int u = 0; u < UN; u++) {
             const int q = q0 + u * 32 + lane;
-            cl += __popc(__ballot_sync(0xffffffffu, q < c1 && v[u] <= khi));
-            cr += __popc(__ballot_sync(0xffffffffu, q < c1 && v[u] >= klo));
+            l += __popc(__ballot_sync(0xffffffffu, q < c1 && pv.le(v[u])));
+            r += __popc(__ballot_sync(0xffffffffu, q < c1 && pv.ge(v[u])));
         }
     }
-    int baseL, baseR, totL, totR;
-    tie_excl_scan2(cl, cr, red, &baseL, &baseR, &totL, &totR);
-    int aL = baseL;   // #L before this step
-    int bB = baseR;   // #R before this step
+    *cl = l;
+    *cr = r;
+}
+
+// Writes the positions of the L and R stops in [c0, c1) into posL / posR by
+// rank (aL, bB: stops of each kind before c0 in the active range; totR: R
+// stops in the whole range).  Returns this lane's count of swapped L stops.
+template <class Arr, class Pos, class Pred>
+__device__ __forceinline__ int place_stops(const Arr& A, int c0, int c1, const Pred& pv, int aL, int bB,
+                                           int totR, const Pos& posL, const Pos& posR) {
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    constexpr int UN = QS_TIE_UN;
     int nswap = 0;
     for (int q0 = c0; q0 < c1; q0 += 32 * UN) {
-      uint32_t vv[UN];
+        uint32_t vv[UN];
 #pragma unroll
-      for (int u = 0; u < UN; u++) {
-          const int q = q0 + u * 32 + lane;
-          vv[u] = (q < c1) ? pbits(A[q]) : 0u;
-      }
-#pragma unroll
-      for (int u = 0; u < UN; u++) {
-        const int q = q0 + u * 32 + lane;
-        const bool in = q < c1;
-        const uint32_t v = vv[u];
-        const bool isL = in && v <= khi, isR = in && v >= klo;
-        const unsigned bl = __ballot_sync(0xffffffffu, isL);
-        const unsigned br = __ballot_sync(0xffffffffu, isR);
-        const int a = aL + __popc(bl & lt) + 1;          // #L in [lo, q]
-        const int b = totR - bB - __popc(br & lt);      // #R in [q, hi]
-        if (isL) {
-            posL[a - 1] = q;
-            nswap += (b >= a);
-        }
-        if (isR) posR[b - 1] = q;
-        aL += __popc(bl);
-        bB += __popc(br);
-      }
-    }
-    const int T = tie_sum(nswap, red);
-    __syncthreads();  // posL / posR complete
-    for (int t0 = tid; t0 < T; t0 += 4 * kTieThreads) {
-        int x[4], y[4];
-        unsigned long long ax[4], ay[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int t = t0 + u * kTieThreads;
-            x[u] = (t < T) ? posL[t] : -1;
-            y[u] = (t < T) ? posR[t] : -1;
+        for (int u = 0; u < UN; u++) {
+            const int q = q0 + u * 32 + lane;
+            vv[u] = (q < c1) ? A.key(q) : 0u;
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            if (x[u] >= 0 && x[u] != y[u]) { ax[u] = A[x[u]]; ay[u] = A[y[u]]; }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            if (x[u] >= 0 && x[u] != y[u]) { A[x[u]] = ay[u]; A[y[u]] = ax[u]; }
-        }
-    }
-    if (tid == 0) {
-        int i, j;
-        if (T == 0) {
-            i = posL[0];
-            j = posR[0];
-        } else {
-            const int x = posL[T - 1], y = posR[T - 1];
-            if (x == y) { i = x + 1; j = x - 1; }
-            else if (y == x + 1) { i = y; j = x; }
-            else {
-                const int nl = (T < totL) ? posL[T] : 0x7fffffff;
-                const int nr = (T < totR) ? posR[T] : -0x7fffffff;
-                i = min(nl, y);
-                j = max(nr, x);
+        for (int u = 0; u < UN; u++) {
+            const int q = q0 + u * 32 + lane;
+            const bool in = q < c1;
+            const bool isL = in && pv.le(vv[u]), isR = in && pv.ge(vv[u]);
+            const unsigned bl = __ballot_sync(0xffffffffu, isL);
+            const unsigned br = __ballot_sync(0xffffffffu, isR);
+            const int a = aL + __popc(bl & lt) + 1;      // #L in [lo, q]
+            const int b = totR - bB - __popc(br & lt);  // #R in [q, hi]
+            if (isL) {
+                posL.st(a - 1, q);
+                nswap += (b >= a);
             }
+            if (isR) posR.st(b - 1, q);
+            aL += __popc(bl);
+            bB += __popc(br);
         }
-        sh[0] = i;
-        sh[1] = j;
     }
-    __syncthreads();
-    *oi = sh[0];
-    *oj = sh[1];
-    __syncthreads();
+    return nswap;
+}
+
+// The scans' final (i, j) after T swaps (the serial loop's exit state).
+template <class Pos>
+__device__ __forceinline__ void final_ij(const Pos& posL, const Pos& posR, int T, int totL, int totR,
+                                         int* oi, int* oj) {
+    int i, j;
+    if (T == 0) {
+        i = posL.ld(0);
+        j = posR.ld(0);
+    } else {
+        const int x = posL.ld(T - 1), y = posR.ld(T - 1);
+        if (x == y) { i = x + 1; j = x - 1; }
+        else if (y == x + 1) { i = y; j = x; }
+        else {
+            const int nl = (T < totL) ? posL.ld(T) : 0x7fffffff;
+            const int nr = (T < totR) ? posR.ld(T) : -0x7fffffff;
+            i = min(nl, y);
+            j = max(nr, x);
+        }
+    }
+    *oi = i;
+    *oj = j;
+}
+
+// Swap pairs t in [t0, T) with stride `stride`.
+template <class Arr, class Pos>
+__device__ __forceinline__ void do_swaps(const Arr& A, const Pos& posL, const Pos& posR, int T, int t0,
+                                         int stride) {
+    for (int tb = t0; tb < T; tb += 4 * stride) {
+        int x[4], y[4], ix[4], iy[4];
+        uint32_t kx[4], ky[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int t = tb + u * stride;
+            x[u] = (t < T) ? posL.ld(t) : -1;
+            y[u] = (t < T) ? posR.ld(t) : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (x[u] >= 0 && x[u] != y[u]) {
+                kx[u] = A.key(x[u]); ix[u] = A.index(x[u]);
+                ky[u] = A.key(y[u]); iy[u] = A.index(y[u]);
+            }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (x[u] >= 0 && x[u] != y[u]) { A.put(x[u], ky[u], iy[u]); A.put(y[u], kx[u], ix[u]); }
+    }
 }
 
 // The reference's probability of a scaled logit t (sampler.h:197-206).
@@ -211,39 +247,85 @@ __device__ __forceinline__ float prob_of(float t, const RowResult& rr, const Exp
     return __fmul_rn(ref_expf(__fsub_rn(t, rr.max_logit), fx), rr.sum_inv);
 }
 
-// [klo, khi]: the order keys of all t with prob_of(t) == prob_of(pivot).
-// prob_of is monotone non-decreasing, so both ends are found by galloping
-// from the pivot's key and bisecting (at most ~64 evaluations, usually 2).
-__device__ void prob_key_interval(uint32_t kp, const RowResult& rr, const ExpFix& fx,
-                                  uint32_t* klo, uint32_t* khi) {
+__device__ __forceinline__ bool same_prob(uint64_t k, float P, const RowResult& rr, const ExpFix& fx) {
+    if (k > 0xFFFFFFFFull) return false;
+    const float t = fkey_inv((uint32_t)k);
+    return t == t && prob_of(t, rr, fx) == P;
+}
+
+// [klo, khi]: the order keys of all t with prob_of(t) == prob_of(pivot), by
+// one warp (every lane returns both).  prob_of is monotone non-decreasing, so
+// each end is found by a 32-ary search: the lanes test 32 keys a step apart,
+// the step grows 32-fold while all match and shrinks 32-fold once one does
+// not.  Usually one evaluation per lane settles both ends.
+__device__ void prob_key_interval_warp(uint32_t kp, const RowResult& rr, const ExpFix& fx,
+                                       uint32_t* klo, uint32_t* khi) {
+    const int lane = threadIdx.x & 31;
     const float P = prob_of(fkey_inv(kp), rr, fx);
-    auto same = [&](uint32_t k) {
-        const float t = fkey_inv(k);
-        return t == t && prob_of(t, rr, fx) == P;
-    };
     if (!(P == P)) { *klo = kp; *khi = kp; return; }
+    // first look: 16 keys above and 16 below the pivot's
+    const uint64_t k1 = (lane < 16) ? (uint64_t)kp + (uint64_t)(lane + 1)
+                                    : ((uint64_t)kp >= (uint64_t)(lane - 15) ? (uint64_t)kp - (uint64_t)(lane - 15)
+                                                                             : (uint64_t)1 << 40);
+    const bool ok1 = same_prob(k1, P, rr, fx);
+    const unsigned m = __ballot_sync(0xffffffffu, !ok1);
     // upward
-    uint32_t good = kp, step = 1;
-    while (good < 0xFFFFFFFFu - step && same(good + step)) { good += step; step <<= 1; }
-    uint32_t bad = (good < 0xFFFFFFFFu - step) ? good + step : 0xFFFFFFFFu;
-    while (bad - good > 1) { const uint32_t mid = good + (bad - good) / 2; if (same(mid)) good = mid; else bad = mid; }
-    *khi = good;
-    // downward
-    good = kp; step = 1;
-    while (good > step && same(good - step)) { good -= step; step <<= 1; }
-    bad = (good > step) ? good - step : 0u;
-    while (good - bad > 1) { const uint32_t mid = bad + (good - bad) / 2; if (same(mid)) good = mid; else bad = mid; }
-    *klo = good;
+    uint64_t good;
+    if (m & 0xFFFFu) {
+        good = (uint64_t)kp + (uint64_t)(__ffs(m & 0xFFFFu) - 1);
+    } else {
+        good = (uint64_t)kp + 16;
+        uint64_t step = 1;
+        bool grow = true;
+        for (int it = 0; it < 64; it++) {
+            const uint64_t cand = good + step * (uint64_t)(lane + 1);
+            const unsigned bad = __ballot_sync(0xffffffffu, !same_prob(cand, P, rr, fx));
+            if (!bad) {
+                good += step * 32;
+                if (grow) step *= 32;
+                continue;
+            }
+            grow = false;
+            good += step * (uint64_t)(__ffs(bad) - 1);
+            if (step == 1) break;
+            step /= 32;
+        }
+    }
+    *khi = (uint32_t)min(good, (uint64_t)0xFFFFFFFFull);
+    // downward (keys below kp, as distances d: kp - d)
+    uint64_t gd;
+    if (m >> 16) {
+        gd = (uint64_t)(__ffs(m >> 16) - 1);
+    } else {
+        gd = 16;
+        uint64_t step = 1;
+        bool grow = true;
+        for (int it = 0; it < 64; it++) {
+            const uint64_t d = gd + step * (uint64_t)(lane + 1);
+            const uint64_t cand = (d <= (uint64_t)kp) ? (uint64_t)kp - d : (uint64_t)1 << 40;
+            const unsigned bad = __ballot_sync(0xffffffffu, !same_prob(cand, P, rr, fx));
+            if (!bad) {
+                gd += step * 32;
+                if (grow) step *= 32;
+                continue;
+            }
+            grow = false;
+            gd += step * (uint64_t)(__ffs(bad) - 1);
+            if (step == 1) break;
+            step /= 32;
+        }
+    }
+    *klo = (uint32_t)((uint64_t)kp - min(gd, (uint64_t)kp));
 }
 
 __device__ void tie_sort_desc(unsigned long long* a, int n) {
     for (int size = 2; size <= n; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
             for (int i = threadIdx.x; i < n / 2; i += kTieThreads) {
-                int lo = 2 * stride * (i / stride) + (i % stride);
-                int hi = lo + stride;
-                bool desc = ((lo & size) == 0);
-                unsigned long long x = a[lo], y = a[hi];
+                const int lo = 2 * stride * (i / stride) + (i % stride);
+                const int hi = lo + stride;
+                const bool desc = ((lo & size) == 0);
+                const unsigned long long x = a[lo], y = a[hi];
                 if ((x < y) == desc) { a[lo] = y; a[hi] = x; }
             }
             __syncthreads();
@@ -251,8 +333,29 @@ __device__ void tie_sort_desc(unsigned long long* a, int n) {
     }
 }
 
+// One partition round on [lo, hi] by one CTA (shared or global arrays).
+template <class Arr, class Pos, class Pred>
+__device__ void cta_round(const Arr& A, const Pos& posL, const Pos& posR, int lo, int hi,
+                          const Pred& pv, int* red, int* oi, int* oj) {
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int n = hi - lo + 1;
+    const int per = (n + kTieWarps - 1) / kTieWarps;
+    const int c0 = lo + warp * per;
+    const int c1 = min(c0 + per, hi + 1);
+    int cl, cr;
+    count_stops(A, c0, c1, pv, &cl, &cr);
+    int baseL, baseR, totL, totR;
+    tie_warp_scan2(cl, cr, red, &baseL, &baseR, &totL, &totR);
+    const int nswap = place_stops(A, c0, c1, pv, baseL, baseR, totR, posL, posR);
+    const int T = tie_cta_sum(nswap, red);
+    __syncthreads();  // posL / posR complete
+    do_swaps(A, posL, posR, T, tid, kTieThreads);
+    final_ij(posL, posR, T, totL, totR, oi, oj);
+    __syncthreads();
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kTieThreads)
+__global__ void __cluster_dims__(kTieCluster, 1, 1) __launch_bounds__(kTieThreads, 3)
 ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __restrict__ ov_n,
             const int* __restrict__ ov_idx, const float* __restrict__ ov_val, int ov_stride,
             const int* __restrict__ slow_list, const int* __restrict__ slow_count,
@@ -261,24 +364,36 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             float* __restrict__ cand_prob_out, int cand_cap, ExpFix fx,
             long long* __restrict__ phase_cycles) {
     __shared__ int red[160];
-    __shared__ int sh[4];
+    __shared__ int xch[4];        // this CTA's L count, R count, swapped count (read by peers)
+    __shared__ uint32_t sh_key[2];
     extern __shared__ __align__(16) unsigned char dyn[];
-    unsigned long long* sA = reinterpret_cast<unsigned long long*>(dyn);   // [kTieSmemRange]
-    unsigned long long* sk = sA + kTieSmemRange;                           // [kCandCap]
-    int* ovi = reinterpret_cast<int*>(sk + kCandCap);
+    uint32_t* sK = reinterpret_cast<uint32_t*>(dyn);                        // [kTieSmemRange]
+    int* sI = reinterpret_cast<int*>(sK + kTieSmemRange);                   // [kTieSmemRange]
+    int* sposL = sI + kTieSmemRange;                                        // [kTieSmemRange]
+    int* sposR = sposL + kTieSmemRange;                                     // [kTieSmemRange]
+    unsigned long long* sk = reinterpret_cast<unsigned long long*>(sposR + kTieSmemRange);  // [kTieSortCap]
+    int* ovi = reinterpret_cast<int*>(sk + kTieSortCap);
     float* ovv = reinterpret_cast<float*>(ovi + (ov_stride > 0 ? ov_stride : 1));
 
-    const int tid = threadIdx.x;
-    unsigned long long* A = scratch + (size_t)blockIdx.x * V;
-    int* posL = pos_scratch + (size_t)blockIdx.x * 2 * V;
-    int* posR = posL + V;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int crank = (int)cluster.block_rank();
+    const int cid = blockIdx.x / kTieCluster;
+    const int ncl = gridDim.x / kTieCluster;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const GlobalArr A{reinterpret_cast<uint32_t*>(scratch + (size_t)cid * V),
+                      reinterpret_cast<int*>(scratch + (size_t)cid * V) + V};
+    const GlobalPos gposL{pos_scratch + (size_t)cid * 2 * V};
+    const GlobalPos gposR{pos_scratch + (size_t)cid * 2 * V + V};
     const int nslow = *slow_count;
     const int k = prm.top_k;
+    int* peer_xch[kTieCluster];
+#pragma unroll
+    for (int r = 0; r < kTieCluster; r++) peer_xch[r] = cluster.map_shared_rank(xch, r);
 
-    for (int li = blockIdx.x; li < nslow; li += gridDim.x) {
+    for (int li = cid; li < nslow; li += ncl) {
         const int row = slow_list[li];
         long long* ph = phase_cycles ? phase_cycles + (size_t)li * 8 : nullptr;
-        if (ph && tid == 0) ph[0] = clock64();
+        if (ph && crank == 0 && tid == 0) ph[0] = clock64();
         const RowResult rr = res[row];
         const T* L = logits + (size_t)row * V;
         const int nov = ov_n ? ov_n[row] : 0;
@@ -287,125 +402,192 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             ovv[i] = ov_val[(size_t)row * ov_stride + i];
         }
         __syncthreads();
-        // the row's values in index order, as order keys of t (sampler.h:184-201)
-        for (int i = tid; i < V; i += kTieThreads) {
-            const float l = Elem<T>::widen(L[i]);
-            A[i] = ((unsigned long long)fkey(__fmul_rn(l, rr.inv_temp)) << 32) | (unsigned)i;
+        // this CTA's slice of the row's values in index order, as order keys
+        // of t (sampler.h:184-201), overrides substituted
+        {
+            const int per = (V + kTieCluster - 1) / kTieCluster;
+            const int s0 = crank * per, s1 = min(s0 + per, V);
+            for (int i = s0 + tid; i < s1; i += kTieThreads) {
+                const float l = Elem<T>::widen(L[i]);
+                A.put(i, fkey(__fmul_rn(l, rr.inv_temp)), i);
+            }
+            __syncthreads();
+            for (int j = tid; j < nov; j += kTieThreads) {
+                const int q = ovi[j];
+                if (q >= s0 && q < s1)
+                    A.put(q, fkey(__fmul_rn(ovv[j], rr.inv_temp)), q);
+            }
         }
-        __syncthreads();
-        for (int j = tid; j < nov; j += kTieThreads)
-            A[ovi[j]] = ((unsigned long long)fkey(__fmul_rn(ovv[j], rr.inv_temp)) << 32) | (unsigned)ovi[j];
-        __syncthreads();
-        if (ph && tid == 0) ph[1] = clock64();
-        // quick_select(probindex, V, k - 1)  (sampler.h:76-94)
+        cluster.sync();
+        if (ph && crank == 0 && tid == 0) ph[1] = clock64();
+
+        // quick_select(probindex, V, k - 1)  (sampler.h:76-94): large ranges
+        // by the whole cluster
         int lo = 0, hi = V - 1;
         const int kk = k - 1;
-        long long rounds = 0;
-        const long long max_rounds = 4ll * V + 64;  // the serial loop needs far fewer
-        unsigned long long* W = A;  // the array the rounds work on
-        int woff = 0, wn = 0;       // W[q - woff] holds position q, for wn positions
-        while (lo < hi && rounds++ < max_rounds) {
-            if (W == A && hi - lo + 1 <= kTieSmemRange) {
-                if (ph && tid == 0) { ph[2] = clock64(); ph[6] = rounds; }
-                // continue in shared memory; positions outside [lo, hi] never move again
-                for (int q = lo + tid; q <= hi; q += kTieThreads) sA[q - lo] = A[q];
-                __syncthreads();
-                W = sA;
-                woff = lo;
-                wn = hi - lo + 1;
-            }
-            if (tid == 0) {
-                const uint32_t kp = pbits(W[kk - woff]);
+        int rounds = 0;
+        const int max_rounds = 2 * V + 64;  // the serial loop needs far fewer
+        while (lo < hi && hi - lo + 1 > kTieSmemRange && rounds < max_rounds) {
+            rounds++;
+            if (warp == 0) {
                 uint32_t klo, khi;
-                prob_key_interval(kp, rr, fx, &klo, &khi);
-                sh[2] = (int)klo;
-                sh[3] = (int)khi;
+                prob_key_interval_warp(A.key(kk), rr, fx, &klo, &khi);
+                if (lane == 0) { sh_key[0] = klo; sh_key[1] = khi; }
             }
             __syncthreads();
-            const uint32_t klo = (uint32_t)sh[2], khi = (uint32_t)sh[3];
+            const KeyPivot pv{sh_key[0], sh_key[1]};
+            const int n = hi - lo + 1;
+            const int cper = (n + kTieCluster - 1) / kTieCluster;
+            const int s0 = min(lo + crank * cper, hi + 1);
+            const int s1 = min(s0 + cper, hi + 1);
+            const int wper = (s1 - s0 + kTieWarps - 1) / kTieWarps;
+            const int c0 = min(s0 + warp * wper, s1);
+            const int c1 = min(c0 + wper, s1);
+            int cl, cr;
+            count_stops(A, c0, c1, pv, &cl, &cr);
+            int wbL, wbR, ctaL, ctaR;
+            tie_warp_scan2(cl, cr, red, &wbL, &wbR, &ctaL, &ctaR);
+            if (tid == 0) { xch[0] = ctaL; xch[1] = ctaR; }
+            cluster.sync();
+            int baseL = 0, baseR = 0, totL = 0, totR = 0;
+#pragma unroll
+            for (int r = 0; r < kTieCluster; r++) {
+                const int xl = peer_xch[r][0], xr = peer_xch[r][1];
+                if (r < crank) { baseL += xl; baseR += xr; }
+                totL += xl;
+                totR += xr;
+            }
+            const int nswap = place_stops(A, c0, c1, pv, baseL + wbL, baseR + wbR, totR, gposL, gposR);
+            const int ctaS = tie_cta_sum(nswap, red);
+            if (tid == 0) xch[2] = ctaS;
+            cluster.sync();
+            int Tsw = 0;
+#pragma unroll
+            for (int r = 0; r < kTieCluster; r++) Tsw += peer_xch[r][2];
+            do_swaps(A, gposL, gposR, Tsw, crank * kTieThreads + tid, kTieCluster * kTieThreads);
             int i, j;
-            partition_round(W - woff, lo, hi, klo, khi, posL, posR, red, sh, &i, &j);
+            final_ij(gposL, gposR, Tsw, totL, totR, &i, &j);
+            cluster.sync();
             if (j < kk) lo = i;
             if (i > kk) hi = j;
+            // the reference keeps lo <= k-1 <= hi; anything else ends the
+            // loop (identically in every CTA: all read the same values)
+            if (lo < 0 || hi >= V || kk < lo || kk > hi) break;
         }
-        if (W != A) {
-            // write the shared-memory range back
-            for (int q = tid; q < wn; q += kTieThreads) A[woff + q] = sA[q];
+        if (ph && crank == 0 && tid == 0) { ph[2] = clock64(); ph[6] = rounds; }
+        // the rest is the first CTA's; when this cluster has no further row
+        // the others leave now (none of them touches a peer's shared memory
+        // again, and no cluster barrier follows), freeing their SMs
+        const bool more = li + ncl < nslow;
+        if (!more && crank != 0) return;
+
+        if (crank == 0) {
+            // small ranges: this CTA alone, in shared memory (positions
+            // outside [lo, hi] never move again)
+            const int woff = lo, wn = hi - lo + 1;
+            const bool in_smem = lo < hi && wn <= kTieSmemRange;
+            if (in_smem) {
+                // the range's exact probabilities (sampler.h:197-206): the
+                // remaining rounds compare them as the reference does
+                for (int q = tid; q < wn; q += kTieThreads) {
+                    sK[q] = __float_as_uint(prob_of(fkey_inv(A.key(woff + q)), rr, fx));
+                    sI[q] = A.index(woff + q);
+                }
+                __syncthreads();
+                const SharedArr S{sK - woff, sI - woff};
+                const SharedPos pL{sposL}, pR{sposR};
+                while (lo < hi && rounds < max_rounds) {
+                    rounds++;
+                    const ProbPivot pv{__uint_as_float(S.key(kk))};
+                    int i, j;
+                    cta_round(S, pL, pR, lo, hi, pv, red, &i, &j);
+                    if (j < kk) lo = i;
+                    if (i > kk) hi = j;
+                    if (lo < woff || hi >= woff + wn || kk < lo || kk > hi) break;
+                }
+                // the range's final arrangement (indices; the keys are not read again)
+                for (int q = tid; q < wn; q += kTieThreads) __stcg(A.idx + woff + q, sI[q]);
+                __syncthreads();
+            }
+            if (ph && tid == 0) { ph[3] = clock64(); ph[7] = rounds; }
+            // exact probabilities of the k selected entries (sampler.h:197-206),
+            // then the stable qsort of the first k by probability, descending
+            // (sampler.h:214): keys (p, k-1-position) keep equal p in position order
+            int npow = 1;
+            while (npow < k) npow <<= 1;
+            for (int i = tid; i < npow; i += kTieThreads) {
+                unsigned long long key = 0ull;
+                if (i < k) {
+                    const int q = A.index(i);
+                    float l = Elem<T>::widen(L[q]);
+                    int a = 0, b = nov;  // the override of q, if any (ovi ascending)
+                    while (a < b) { const int m = (a + b) >> 1; if (ovi[m] < q) a = m + 1; else b = m; }
+                    if (a < nov && ovi[a] == q) l = ovv[a];
+                    const float p = prob_of(__fmul_rn(l, rr.inv_temp), rr, fx);
+                    key = ((unsigned long long)__float_as_uint(p) << 32) |
+                          (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+                }
+                sk[i] = key;
+            }
             __syncthreads();
-        }
-        if (ph && tid == 0) { ph[3] = clock64(); ph[7] = rounds; }
-        // exact probabilities of the k selected entries (sampler.h:197-206)
-        for (int i = tid; i < k; i += kTieThreads) {
-            const float t = fkey_inv(pbits(A[i]));
-            const float p = __fmul_rn(ref_expf(__fsub_rn(t, rr.max_logit), fx), rr.sum_inv);
-            A[i] = ((unsigned long long)__float_as_uint(p) << 32) | (A[i] & 0xFFFFFFFFull);
-        }
-        __syncthreads();
-        // stable qsort of the first k by probability, descending (sampler.h:214)
-        int npow = 1;
-        while (npow < k) npow <<= 1;
-        for (int i = tid; i < npow; i += kTieThreads) {
-            sk[i] = (i < k) ? (((unsigned long long)pbits(A[i]) << 32) |
-                               (unsigned long long)(0xFFFFFFFFu - (uint32_t)i))
-                            : 0ull;
-        }
-        __syncthreads();
-        tie_sort_desc(sk, npow);
-        // min-p, top-p, renormalise, draw on the exact order (thread 0)
-        if (tid == 0) {
-            auto P = [&](int i) { return __uint_as_float((uint32_t)(sk[i] >> 32)); };
-            auto I = [&](int i) {
-                const int pos = (int)(0xFFFFFFFFu - (uint32_t)(sk[i] & 0xFFFFFFFFull));
-                return (int)(uint32_t)(A[pos] & 0xFFFFFFFFull);
-            };
-            int n = k;
-            if (prm.minp > 0.0f) {
-                float pmax = P(0);
-                for (int i = 1; i < n; i++) if (P(i) > pmax) pmax = P(i);
-                const float thrp = __fmul_rn(prm.minp, pmax);
-                int kept = 0;
-                while (kept < n && P(kept) >= thrp) kept++;
-                n = kept > 0 ? kept : 1;
-            }
-            const int n_minp = n;
-            if (prm.topp < 1.0f && prm.topp > 0.0f) {
+            tie_sort_desc(sk, npow);
+            // min-p, top-p, renormalise, draw on the exact order (thread 0)
+            if (tid == 0) {
+                auto P = [&](int i) { return __uint_as_float((uint32_t)(sk[i] >> 32)); };
+                auto I = [&](int i) {
+                    const int pos = (int)(0xFFFFFFFFu - (uint32_t)(sk[i] & 0xFFFFFFFFull));
+                    return A.index(pos);
+                };
+                int n = k;
+                if (prm.minp > 0.0f) {
+                    float pmax = P(0);
+                    for (int i = 1; i < n; i++) if (P(i) > pmax) pmax = P(i);
+                    const float thrp = __fmul_rn(prm.minp, pmax);
+                    int kept = 0;
+                    while (kept < n && P(kept) >= thrp) kept++;
+                    n = kept > 0 ? kept : 1;
+                }
+                const int n_minp = n;
+                if (prm.topp < 1.0f && prm.topp > 0.0f) {
+                    float cum = 0.f;
+                    int cut = 0;
+                    for (int i = 0; i < n; i++) {
+                        cum = __fadd_rn(cum, P(i));
+                        if (cum >= prm.topp) { cut = i + 1; break; }
+                    }
+                    if (cut > 0) n = cut;
+                }
+                float s2 = 0.f;
+                for (int i = 0; i < n; i++) s2 = __fadd_rn(s2, P(i));
+                const float inv2 = __fdiv_rn(1.0f, s2);
                 float cum = 0.f;
-                int cut = 0;
+                int pos = n - 1;
                 for (int i = 0; i < n; i++) {
-                    cum = __fadd_rn(cum, P(i));
-                    if (cum >= prm.topp) { cut = i + 1; break; }
+                    cum = __fadd_rn(cum, __fmul_rn(P(i), inv2));
+                    if (rr.r < cum) { pos = i; break; }
                 }
-                if (cut > 0) n = cut;
-            }
-            float s2 = 0.f;
-            for (int i = 0; i < n; i++) s2 = __fadd_rn(s2, P(i));
-            const float inv2 = __fdiv_rn(1.0f, s2);
-            float cum = 0.f;
-            int pos = n - 1;
-            for (int i = 0; i < n; i++) {
-                cum = __fadd_rn(cum, __fmul_rn(P(i), inv2));
-                if (rr.r < cum) { pos = i; break; }
-            }
-            if (ph) ph[4] = clock64();
-            RowResult o = rr;
-            o.token = I(pos);
-            o.n_topk = k;
-            o.n_minp = n_minp;
-            o.n_final = n;
-            o.renorm_sum = s2;
-            o.draw_pos = pos;
-            o.exact_ties = 1;
-            o.status = 0;
-            res[row] = o;
-            if (cand_index_out) {
-                const int lim = min(k, cand_cap);
-                for (int i = 0; i < lim; i++) {
-                    cand_index_out[(size_t)row * cand_cap + i] = I(i);
-                    cand_prob_out[(size_t)row * cand_cap + i] = i < n ? __fmul_rn(P(i), inv2) : P(i);
+                if (ph) ph[4] = clock64();
+                RowResult o = rr;
+                o.token = I(pos);
+                o.n_topk = k;
+                o.n_minp = n_minp;
+                o.n_final = n;
+                o.renorm_sum = s2;
+                o.draw_pos = pos;
+                o.exact_ties = 1;
+                o.status = 0;
+                res[row] = o;
+                if (cand_index_out) {
+                    const int lim = min(k, cand_cap);
+                    for (int i = 0; i < lim; i++) {
+                        cand_index_out[(size_t)row * cand_cap + i] = I(i);
+                        cand_prob_out[(size_t)row * cand_cap + i] = i < n ? __fmul_rn(P(i), inv2) : P(i);
+                    }
                 }
             }
         }
-        __syncthreads();
+        // the scratch and the exchange slots are reused by the next row
+        if (more) cluster.sync();
     }
 }
 
@@ -413,18 +595,22 @@ template <typename T>
 cudaError_t launch_ties_kernel(const T* logits, int V, TieParams prm, const int* ov_n,
                                const int* ov_idx, const float* ov_val, int ov_stride,
                                const int* slow_list, const int* slow_count, RowResult* res,
-                               unsigned long long* scratch, int* pos_scratch, int nctas,
+                               unsigned long long* scratch, int* pos_scratch, int nslots,
                                int* cand_index, float* cand_prob, int cand_cap, ExpFix fx,
                                cudaStream_t stream, long long* phase_cycles) {
-    const size_t smem = 8 * (size_t)kTieSmemRange + 8 * (size_t)kCandCap +
+    const size_t smem = 16 * (size_t)kTieSmemRange + 8 * (size_t)kTieSortCap +
                         8 * (size_t)(ov_stride > 0 ? ov_stride : 1) + 16;
     cudaError_t err = cudaFuncSetAttribute(ties_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err != cudaSuccess) return err;
-    ties_kernel<T><<<nctas, kTieThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val,
-                                                         ov_stride, slow_list, slow_count, res,
-                                                         scratch, pos_scratch, cand_index,
-                                                         cand_prob, cand_cap, fx, phase_cycles);
+    // one scratch slot (V keys, 2V positions) per cluster; clusters beyond the
+    // queued rows exit at once, and those beyond what the GPU holds at a time
+    // start as earlier ones finish
+    const int ncl = nslots;
+    if (ncl < 1) return cudaSuccess;
+    ties_kernel<T><<<ncl * kTieCluster, kTieThreads, smem, stream>>>(
+        logits, V, prm, ov_n, ov_idx, ov_val, ov_stride, slow_list, slow_count, res, scratch,
+        pos_scratch, cand_index, cand_prob, cand_cap, fx, phase_cycles);
     return cudaGetLastError();
 }
 
