@@ -150,13 +150,16 @@ def cpu_reference_sample(target_s: float = 15.0, seed: int = 4):
     rows = int(max(probe.batch, min(2048, target_s / max(per_row, 1e-6))))
     wl = W.topk_bf16(B=rows, seed=seed + 100)
     wx = wl.logits_f32()
+    # the same rows again until about target_s of CPU time (threads x wall) is spent
+    reps = max(1, min(16, int(target_s / max(per_row * rows * threads, 1e-6))))
     t0 = time.perf_counter()
-    run(wl, wx)
+    for _ in range(reps):
+        run(wl, wx)
     dt = time.perf_counter() - t0
-    return {"value": rows / dt, "unit": "rows/s", "cores": threads, "kind": kind,
-            "sample": f"{rows} rows of the benchmark workload (seed {seed + 100}), "
+    return {"value": reps * rows / dt, "unit": "rows/s", "cores": threads, "kind": kind,
+            "sample": f"{rows} rows of the benchmark workload (seed {seed + 100}) x {reps}, "
                       f"{dt:.1f} s on {threads} host threads",
-            "seconds": dt, "rows": rows}
+            "seconds": dt, "rows": reps * rows}
 
 
 def run_reference_arm(args):
@@ -235,6 +238,9 @@ def main():
     import torch.distributed as dist
     from datetime import timedelta
 
+    import numpy as np
+
+    from qwen600_engine_b200 import shard
     from qwen600_engine_b200.sampler import Sampler
 
     rank = int(os.environ.get("RANK", "0"))
@@ -248,7 +254,9 @@ def main():
 
     bufs = [make_inputs(torch, B, 4 + 7919 * rank + 104729 * i, dev) for i in range(2)]
     hist, counts, count = bufs[0][1], bufs[0][2], bufs[0][3]
-    rng = bufs[0][4].clone()
+    # this rank's block of the world x B batch keeps the global rows' RNG streams
+    a, b = shard.row_block(rank, world, world * B)
+    rng = torch.from_numpy(shard.row_seeds(4, a, b).view(np.int64)).to(dev)
     toks = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
     glist = [[torch.empty(B, dtype=torch.int32, device=dev) for _ in range(world)]
              for _ in range(2)] if (world > 1 and rank == 0) else [None, None]
@@ -301,9 +309,7 @@ def main():
     launches = int(prof1["launches"] - prof0["launches"])
     sync_all()
     if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = shard.max_over_ranks(ms, device=dev)
     ms_step = ms / args.steps
     value = world * B / (ms_step / 1e3)
 
@@ -360,9 +366,7 @@ def main():
         torch.cuda.synchronize()
         ems = a.elapsed_time(b)
         if world > 1:
-            t = torch.tensor([ems], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
+            ems = shard.max_over_ranks(ems, device=dev)
         h2d = (bufs[0][0].numel() * 2 + hist.numel() * 4 + counts.numel() * 4 + count.numel() * 4
                + rng.numel() * 8)
         e2e = {"value": world * B / (ems / args.e2e_steps / 1e3), "unit": "rows/s",

@@ -169,7 +169,11 @@ class RefSampler:
         L.ref_session_token_count.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.ref_session_reset.argtypes = [C.c_void_p]
         L.ref_session_free.argtypes = [C.c_void_p]
+        L.ref_session_set_rng.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
         self.vocab = L.ref_vocab_size()
+
+    def session(self, params, batch: int, window: int, seeds) -> "RefSession":
+        return RefSession(self, params, batch, window, seeds)
 
     def sample_rows(self, params, logits_f32, hist=None, hist_counts=None, hist_count=None,
                     hist_pos=None, rng=None, want_mutated=False, want_probindex=False,
@@ -208,6 +212,69 @@ class RefSampler:
     def sample_workload(self, wl, **kw):
         return self.sample_rows(wl.params, wl.logits_f32(), wl.hist, wl.hist_counts,
                                 wl.hist_count, wl.hist_pos, wl.rng, **kw)
+
+
+class RefSession:
+    """``batch`` persistent reference Samplers driven step by step, as
+    main.cu's decode loop drives one (main.cu:136-139): each step samples every
+    row and the reference updates the row's history itself (sampler.h:257-267)."""
+
+    def __init__(self, ref: RefSampler, params, batch: int, window: int, seeds):
+        self.ref = ref
+        self.batch = int(batch)
+        self.window = int(window)
+        sd = np.ascontiguousarray(np.asarray(seeds, dtype=np.uint64).reshape(-1))
+        if sd.shape[0] != self.batch:
+            raise ValueError("one seed per row")
+        self.h = ref.lib.ref_session_create(self.batch, params.temperature, params.topp,
+                                            params.minp, int(params.top_k),
+                                            params.repetition_penalty, params.frequency_penalty,
+                                            params.presence_penalty, self.window,
+                                            _ptr(sd, C.c_uint64))
+
+    def step(self, logits_f32: np.ndarray, n_threads: int = 1) -> np.ndarray:
+        x = np.ascontiguousarray(logits_f32, dtype=np.float32)
+        out = np.zeros(self.batch, dtype=np.int32)
+        rc = self.ref.lib.ref_session_step(self.h, _ptr(x, C.c_float), int(x.shape[1]),
+                                           _ptr(out, C.c_int), None, n_threads)
+        if rc != 0:
+            raise RuntimeError(f"reference session rejected the step: {rc}")
+        return out
+
+    def set_params(self, params) -> None:
+        self.ref.lib.ref_session_set_params(self.h, params.temperature, params.topp, params.minp,
+                                            int(params.top_k), params.repetition_penalty,
+                                            params.frequency_penalty, params.presence_penalty)
+
+    def set_rng(self, r: int, state: int) -> None:
+        self.ref.lib.ref_session_set_rng(self.h, int(r), C.c_uint64(int(state)))
+
+    def state(self, r: int):
+        rng = C.c_uint64()
+        cnt = C.c_int()
+        pos = C.c_int()
+        ring = np.zeros(max(self.window, 1), dtype=np.int32)
+        self.ref.lib.ref_session_state(self.h, int(r), C.byref(rng), C.byref(cnt), C.byref(pos),
+                                       _ptr(ring, C.c_int), self.window)
+        return {"rng": int(rng.value), "count": cnt.value, "pos": pos.value,
+                "ring": ring[:self.window].copy()}
+
+    def token_count(self, r: int, token: int) -> float:
+        return float(self.ref.lib.ref_session_token_count(self.h, int(r), int(token)))
+
+    def reset(self) -> None:
+        self.ref.lib.ref_session_reset(self.h)
+
+    def free(self) -> None:
+        if self.h:
+            self.ref.lib.ref_session_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 def ref_available() -> bool:

@@ -164,6 +164,12 @@ void ref_session_state(void* h, int r, unsigned long long* rng, int* count, int*
     for (int i = 0; i < W && s.recent_tokens; i++) ring[i] = s.recent_tokens[i];
 }
 
+// Mirrors python/bindings.cu:236-238 (sampler.rng_state = seed).
+void ref_session_set_rng(void* h, int r, unsigned long long state) {
+    RefSession* rs = (RefSession*)h;
+    rs->s[r].rng_state = state;
+}
+
 float ref_session_token_count(void* h, int r, int token) {
     RefSession* rs = (RefSession*)h;
     return rs->s[r].token_counts ? rs->s[r].token_counts[token] : 0.0f;

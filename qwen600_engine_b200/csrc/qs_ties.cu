@@ -44,7 +44,7 @@ constexpr int kTieWarps = kTieThreads / 32;
 constexpr int kTieSmemRange = 2048;      // active ranges up to this size continue in shared memory
 constexpr int kTieSortCap = kCandCap / 2; // top-k limit of the API: the sorted prefix fits
 #ifndef QS_TIE_UN
-#define QS_TIE_UN 16
+#define QS_TIE_UN 8
 #endif
 
 // Exclusive scan over the CTA's warps of two per-warp counts (valid in lane
