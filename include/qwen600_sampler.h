@@ -195,6 +195,39 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
                                  float repetition_penalty, float frequency_penalty,
                                  float presence_penalty, int* d_tokens, void* stream);
 
+/* The decode step's tail before sampling: final RMSNorm and lm_head.
+ * Replaces qwen_model.cuh:710-723 (rmsnorm_gpu on the final hidden state,
+ * rms_norm_kernel qwen_model.cuh:125-177, then matmul_cublas
+ * qwen_model.cuh:607-629 with bf16 inputs and output and fp32 compute), for
+ * `batch` hidden rows at once:
+ *   normed[b] = bf16((x * rsqrt(fma(sum(x^2), 1/D, 1e-6))) * norm_weight)
+ *   logits[b] = bf16(normed[b] . W^T)          (fp32 accumulation)
+ * d_hidden bf16 [batch, hidden_dim], d_norm_weight bf16 [hidden_dim] (NULL =
+ * ones), d_weight bf16 [vocab, hidden_dim] (the tied embedding / lm_head),
+ * d_normed bf16 [batch, hidden_dim] and d_logits bf16 [batch, vocab] outputs;
+ * all 16-byte aligned; hidden_dim a multiple of 64.  Each block of 128 rows
+ * reads W once.  d_error_flag (device int, zero on entry; NULL = one inside
+ * the library) is set to 1 if the kernel gave up waiting on its own pipeline,
+ * which a correct build never does.  Allocates nothing.  No counterpart
+ * entry point in the reference (it calls the two steps inside forward()). */
+QS_API int qs_lm_head(const void* d_hidden, const void* d_norm_weight, const void* d_weight,
+                      int batch, int hidden_dim, int vocab, void* d_normed, void* d_logits,
+                      int* d_error_flag, void* stream);
+
+/* qs_lm_head into the handle's workspace followed by qs_sample on the
+ * resulting bf16 logits: the reference's forward() tail plus sample()
+ * (main.cu:138-139) for a batch, without the fp32 widening and the host copy
+ * of qwen_model.cuh:717-723.  The first call (and a call with a new
+ * hidden_dim) allocates the workspace: max_batch x (hidden_dim + vocab) bf16.
+ * qs_lm_head_logits returns that logits buffer (for inspection);
+ * qs_lm_head_status synchronises `stream` and reports (and clears) the
+ * kernel's give-up flag. */
+QS_API int qs_lm_head_sample(qs_sampler* s, const void* d_hidden, const void* d_norm_weight,
+                             const void* d_weight, int batch, int hidden_dim, int* d_tokens,
+                             void* stream, unsigned flags);
+QS_API int qs_lm_head_logits(qs_sampler* s, const void** d_logits);
+QS_API int qs_lm_head_status(qs_sampler* s, void* stream);
+
 /* Message for the last error on the calling thread ("" if none). */
 QS_API const char* qs_last_error(void);
 

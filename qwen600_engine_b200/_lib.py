@@ -30,7 +30,8 @@ EXPORTS = (
     "qs_set_rng_state", "qs_get_rng_state", "qs_reset_sampler_history", "qs_sample",
     "qs_sample_rows", "qs_sample_rows_debug", "qs_sample_host", "qs_last_error",
     "qs_max_vocab", "qs_profile_enable", "qs_profile_reset", "qs_profile_read",
-    "qs_argmax_rows_static",
+    "qs_argmax_rows_static", "qs_lm_head", "qs_lm_head_sample", "qs_lm_head_logits",
+    "qs_lm_head_status",
 )
 
 
@@ -87,6 +88,10 @@ def _load() -> C.CDLL:
     lib.qs_profile_read.argtypes = [vp, P(Profile)]
     lib.qs_argmax_rows_static.argtypes = [vp, i32, i32, i32, vp, vp, vp, i32, C.c_float, C.c_float,
                                           C.c_float, vp, vp]
+    lib.qs_lm_head.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp, vp, vp]
+    lib.qs_lm_head_sample.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp, u32]
+    lib.qs_lm_head_logits.argtypes = [vp, P(vp)]
+    lib.qs_lm_head_status.argtypes = [vp, vp]
     lib.qs_last_error.restype = C.c_char_p
     lib.qs_last_error.argtypes = []
     lib.qs_max_vocab.argtypes = []

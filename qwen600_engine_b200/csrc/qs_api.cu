@@ -39,6 +39,11 @@ template <typename T>
 cudaError_t launch_probs(const T*, int, int, const int*, const int*, const float*, int,
                          const RowResult*, float*, ExpFix, cudaStream_t);
 
+cudaError_t launch_lm_head(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int, int,
+                           int, int*, cudaStream_t);
+cudaError_t launch_rmsnorm(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int,
+                           cudaStream_t);
+
 // host copy of the libm expf correction table (generated at build time)
 #include "qs_exp_table.inc"
 
@@ -97,6 +102,12 @@ struct qs_sampler {
     uint32_t* exp_off = nullptr;
     uint32_t* exp_ent = nullptr;
     uint32_t* exp_bloom = nullptr;
+    // lm_head tail (allocated by the first qs_lm_head_sample call)
+    int num_sms = 148;
+    int lh_dim = 0;
+    __nv_bfloat16* lh_normed = nullptr;  // [max_batch, lh_dim]
+    __nv_bfloat16* lh_logits = nullptr;  // [max_batch, vocab]
+    int* lh_err = nullptr;
     ExpFix fix() const { return ExpFix{exp_off, exp_ent, exp_bloom, (uint32_t)QS_EXP_NB}; }
     // launch accounting and optional per-kernel event timing
     bool profiling = false;
@@ -160,7 +171,8 @@ static void release(qs_sampler* s) {
     cudaSetDevice(s->device);
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts,
-                    s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom};
+                    s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
+                    s->lh_normed, s->lh_logits, s->lh_err};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
@@ -227,6 +239,11 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     s->window = penalty_window;
     s->ov_stride = penalty_window > 0 ? penalty_window : 1024;
     s->params = *params;
+    {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
+            s->num_sms = sms;
+    }
     s->tie_ctas = max_batch < 148 ? max_batch : 148;
     const size_t B = (size_t)max_batch, V = (size_t)vocab, W = (size_t)penalty_window;
 #define ALLOC(ptr, bytes)                                                                  \
@@ -550,6 +567,116 @@ int qs_profile_read(qs_sampler* s, qs_profile* out) {
     }
     s->pending.clear();
     *out = s->prof;
+    return QS_OK;
+}
+
+// ---- the decode tail: final RMSNorm + lm_head (qwen_model.cuh:710-723)
+static __device__ int g_lm_head_err;  // error flag of the stateless entry when the caller passes none
+
+static int lm_head_args(const void* d_hidden, const void* d_weight, int batch, int hidden_dim,
+                        int vocab) {
+    if (!d_hidden || !d_weight) return fail(QS_ERR_INVALID, "NULL device pointer");
+    if (batch < 0) return fail(QS_ERR_INVALID, "batch %d < 0", batch);
+    if (hidden_dim < 64 || hidden_dim % 64 != 0)
+        return fail(QS_ERR_UNSUPPORTED, "hidden_dim %d is not a positive multiple of 64", hidden_dim);
+    if (vocab < 1 || vocab > kMaxVocab)
+        return fail(QS_ERR_UNSUPPORTED, "vocab %d outside [1, %d]", vocab, kMaxVocab);
+    if ((((uintptr_t)d_hidden) | ((uintptr_t)d_weight)) & 15)
+        return fail(QS_ERR_INVALID, "hidden and weight must be 16-byte aligned");
+    return QS_OK;
+}
+
+// RMSNorm of `batch` rows, then logits in blocks of 128 rows (each block
+// streams W once).
+static int lm_head_launch(const void* d_hidden, const void* d_norm_weight, const void* d_weight,
+                          int batch, int hidden_dim, int vocab, __nv_bfloat16* normed,
+                          __nv_bfloat16* logits, int* err, int num_sms, cudaStream_t st) {
+    if (batch == 0) return QS_OK;
+    CK(launch_rmsnorm((const __nv_bfloat16*)d_hidden, (const __nv_bfloat16*)d_norm_weight, normed,
+                      batch, hidden_dim, st));
+    for (int r0 = 0; r0 < batch; r0 += 128) {
+        const int rb = batch - r0 < 128 ? batch - r0 : 128;
+        const cudaError_t e = launch_lm_head(normed + (size_t)r0 * hidden_dim,
+                                             (const __nv_bfloat16*)d_weight,
+                                             logits + (size_t)r0 * vocab, rb, vocab, hidden_dim,
+                                             num_sms, err, st);
+        if (e == cudaErrorInvalidValue)
+            return fail(QS_ERR_UNSUPPORTED, "lm_head: the tensor maps of these buffers cannot be built");
+        CK(e);
+    }
+    return QS_OK;
+}
+
+int qs_lm_head(const void* d_hidden, const void* d_norm_weight, const void* d_weight, int batch,
+               int hidden_dim, int vocab, void* d_normed, void* d_logits, int* d_error_flag,
+               void* stream) {
+    g_err.clear();
+    int rc = lm_head_args(d_hidden, d_weight, batch, hidden_dim, vocab);
+    if (rc) return rc;
+    if (!d_normed || !d_logits) return fail(QS_ERR_INVALID, "NULL output buffer");
+    if ((((uintptr_t)d_normed) | ((uintptr_t)d_logits)) & 15)
+        return fail(QS_ERR_INVALID, "normed and logits must be 16-byte aligned");
+    int* err = d_error_flag;
+    if (!err) {
+        void* p = nullptr;
+        CK(cudaGetSymbolAddress(&p, g_lm_head_err));
+        err = (int*)p;
+    }
+    int dev = 0, sms = 148;
+    CK(cudaGetDevice(&dev));
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+        sms = 148;
+    return lm_head_launch(d_hidden, d_norm_weight, d_weight, batch, hidden_dim, vocab,
+                          (__nv_bfloat16*)d_normed, (__nv_bfloat16*)d_logits, err, sms,
+                          (cudaStream_t)stream);
+}
+
+int qs_lm_head_sample(qs_sampler* s, const void* d_hidden, const void* d_norm_weight,
+                      const void* d_weight, int batch, int hidden_dim, int* d_tokens, void* stream,
+                      unsigned flags) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    int rc = lm_head_args(d_hidden, d_weight, batch, hidden_dim, s->vocab);
+    if (rc) return rc;
+    if (batch > s->max_batch) return fail(QS_ERR_INVALID, "batch %d > max_batch %d", batch, s->max_batch);
+    DeviceGuard dg(s->device);
+    if (s->lh_dim != hidden_dim) {
+        // first use (or a new hidden size): the tail's workspace
+        if (s->lh_normed) cudaFree(s->lh_normed);
+        if (s->lh_logits) cudaFree(s->lh_logits);
+        if (s->lh_err) cudaFree(s->lh_err);
+        s->lh_normed = nullptr; s->lh_logits = nullptr; s->lh_err = nullptr; s->lh_dim = 0;
+        CK(cudaMalloc(&s->lh_normed, sizeof(__nv_bfloat16) * (size_t)s->max_batch * hidden_dim));
+        CK(cudaMalloc(&s->lh_logits, sizeof(__nv_bfloat16) * (size_t)s->max_batch * s->vocab));
+        CK(cudaMalloc(&s->lh_err, sizeof(int)));
+        CK(cudaMemset(s->lh_err, 0, sizeof(int)));
+        s->lh_dim = hidden_dim;
+    }
+    rc = lm_head_launch(d_hidden, d_norm_weight, d_weight, batch, hidden_dim, s->vocab, s->lh_normed,
+                        s->lh_logits, s->lh_err, s->num_sms, (cudaStream_t)stream);
+    if (rc) return rc;
+    return qs_sample(s, s->lh_logits, QS_BF16, batch, d_tokens, stream, flags);
+}
+
+int qs_lm_head_logits(qs_sampler* s, const void** d_logits) {
+    g_err.clear();
+    if (!s || !d_logits) return fail(QS_ERR_INVALID, "NULL argument");
+    *d_logits = s->lh_logits;
+    return QS_OK;
+}
+
+int qs_lm_head_status(qs_sampler* s, void* stream) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    if (!s->lh_err) return QS_OK;
+    DeviceGuard dg(s->device);
+    int h = 0;
+    CK(cudaStreamSynchronize((cudaStream_t)stream));
+    CK(cudaMemcpy(&h, s->lh_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) {
+        CK(cudaMemset(s->lh_err, 0, sizeof(int)));
+        return fail(QS_ERR_CUDA, "lm_head kernel gave up waiting (a pipeline wait passed its time limit)");
+    }
     return QS_OK;
 }
 

@@ -1,0 +1,385 @@
+// The decode step's tail before sampling: the final RMSNorm and the lm_head
+// projection (qwen_model.cuh:710-723), on sm_100a.
+//
+// rmsnorm_rows_kernel restates rms_norm_kernel (qwen_model.cuh:125-177) row
+// by row: per-thread fma chains over bf16 pairs, a 256-thread cub block sum,
+// mul = rsqrtf(fma(sum, 1/D, eps)), y = bf16((x * mul) * w).  The reference
+// normalises one row per call; here a CTA per row of the batch.
+//
+// lm_head_kernel computes logits[B, V] = bf16(normed[B, K] . W[V, K]^T) with
+// fp32 accumulation, as the reference's cublasGemmEx call does
+// (qwen_model.cuh:607-629: bf16 inputs and output, fp32 compute).  It is a
+// persistent, warp-specialised tcgen05 GEMM:
+//   warp 0  one thread issues TMA loads (128B-swizzled K-major tiles of the
+//           normed hidden rows and of 256 vocabulary rows of W) into a
+//           4-stage shared-memory ring;
+//   warp 1  one thread issues tcgen05.mma (M = 128 batch rows, N = 256
+//           vocabulary rows, K = 16 per instruction) into one of two TMEM
+//           accumulators, and tcgen05.commit frees each stage and hands
+//           a finished accumulator to the epilogue;
+//   warps 2-5 read the accumulator with tcgen05.ld (each warp its 32 TMEM
+//           lanes = 32 batch rows), round to bf16 and store the logits.
+// W is read from HBM exactly once per launch (311 MB for Qwen3-0.6B: the
+// bound); the hidden rows (at most 256 KB) are re-read from L2 per tile.
+// Every wait is bounded: after kLhWaitNs the kernel raises an error flag,
+// lets the copies and MMAs it issued finish, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cub/block/block_reduce.cuh>
+
+#include "qs_common.cuh"
+
+namespace qs {
+
+constexpr int kLhM = 128;                       // batch rows per launch (MMA M)
+constexpr int kLhN = 256;                       // vocabulary rows per tile (MMA N)
+constexpr int kLhK = 64;                        // K per stage: one 128-byte swizzle row
+constexpr int kLhStages = 4;
+constexpr int kLhThreads = 192;
+constexpr uint32_t kLhStageA = kLhM * kLhK * 2;  // 16 KB
+constexpr uint32_t kLhStageB = kLhN * kLhK * 2;  // 32 KB
+constexpr uint32_t kLhTmemCols = 2 * kLhN;       // two fp32 accumulators
+constexpr unsigned long long kLhWaitNs = 2000000000ull;
+
+// tcgen05.mma kind::f16 instruction descriptor: fp32 accumulator, bf16 A and
+// B, both K-major, N = 256, M = 128.
+constexpr uint32_t kLhIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kLhN >> 3) << 17) |
+                              ((uint32_t)(kLhM >> 4) << 24);
+
+struct LhShared {
+    unsigned long long full[kLhStages];
+    unsigned long long empty[kLhStages];
+    unsigned long long tfull[2];
+    unsigned long long tempty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+size_t lm_head_smem() { return 1024 + kLhStages * (size_t)(kLhStageA + kLhStageB) + sizeof(LhShared); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(unsigned long long* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Waits for the phase of `parity` to complete; false if the kernel is
+// aborting or `limit_ns` passed (then it raises the abort flag).
+__device__ bool mbar_wait(unsigned long long* b, uint32_t parity, volatile int* abort,
+                          unsigned long long limit_ns = kLhWaitNs) {
+    if (mbar_try(b, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 127u) == 0) {
+            if (*abort) return false;
+            if (global_ns() - t0 > limit_ns) {
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, unsigned long long* bar,
+                                            int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+            "r"(smem_u32(dst)),
+        "l"((unsigned long long)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
+// rows are 128 bytes apart (8-row groups 1024 bytes apart).
+__device__ __forceinline__ unsigned long long sw128_desc(uint32_t saddr) {
+    return (unsigned long long)((saddr >> 4) & 0x3FFFu)  // start address
+           | (1ull << 16)                                 // leading byte offset (16 B)
+           | (64ull << 32)                                // stride byte offset (1024 B)
+           | (1ull << 46)                                 // descriptor version (sm_100)
+           | (2ull << 61);                                // 128-byte swizzle
+}
+__device__ __forceinline__ void umma_bf16(uint32_t dtmem, unsigned long long adesc, unsigned long long bdesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
+        "l"(adesc), "l"(bdesc), "r"(kLhIdesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(unsigned long long* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kLhThreads, 1)
+lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               __nv_bfloat16* __restrict__ out, int B, int V, int K, int ntiles, int* __restrict__ err) {
+    extern __shared__ unsigned char lh_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(lh_raw) + 1023) & ~(uintptr_t)1023);
+    unsigned char* sA = base;                              // [stages][128 x 64 bf16]
+    unsigned char* sB = base + kLhStages * kLhStageA;      // [stages][256 x 64 bf16]
+    LhShared* sh = reinterpret_cast<LhShared*>(sB + kLhStages * kLhStageB);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = K / kLhK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kLhStages; s++) {
+            mbar_init(&sh->full[s], 1);
+            mbar_init(&sh->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&sh->tfull[b], 1);
+            mbar_init(&sh->tempty[b], 4);  // one arrival per epilogue warp
+        }
+        sh->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&tmB) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&sh->tmem_base)),
+                     "r"(kLhTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = sh->tmem_base;
+    volatile int* abort = &sh->abort;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer
+            int s = 0;
+            uint32_t ph = 0;
+            int last_ph[kLhStages];
+            for (int i = 0; i < kLhStages; i++) last_ph[i] = -1;
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
+                for (int kb = 0; kb < nk; kb++) {
+                    if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort)) { stop = true; break; }
+                    mbar_expect_tx(&sh->full[s], kLhStageA + kLhStageB);
+                    tma_load_2d(sA + s * kLhStageA, &tmA, &sh->full[s], kb * kLhK, 0);
+                    tma_load_2d(sB + s * kLhStageB, &tmB, &sh->full[s], kb * kLhK, tile * kLhN);
+                    last_ph[s] = (int)ph;
+                    if (++s == kLhStages) { s = 0; ph ^= 1u; }
+                }
+            }
+            if (*abort) {
+                // let the copies this thread issued land before the CTA leaves
+                for (int i = 0; i < kLhStages; i++)
+                    if (last_ph[i] >= 0) mbar_wait(&sh->full[i], (uint32_t)last_ph[i], abort, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            int s = 0;
+            uint32_t ph = 0;
+            unsigned long long* last_bar = nullptr;
+            uint32_t last_par = 0;
+            bool stop = false;
+            int it = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x, it++) {
+                const int b = it & 1;
+                const uint32_t use = (uint32_t)(it >> 1);
+                if (!mbar_wait(&sh->tempty[b], (use & 1u) ^ 1u, abort)) break;
+                tc_fence_after();
+                const uint32_t dt = tbase + (uint32_t)(b * kLhN);
+                for (int kb = 0; kb < nk; kb++) {
+                    if (!mbar_wait(&sh->full[s], ph, abort)) { stop = true; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * kLhStageA);
+                    const uint32_t b0 = smem_u32(sB + s * kLhStageB);
+#pragma unroll
+                    for (int kk = 0; kk < kLhK / 16; kk++)
+                        umma_bf16(dt, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32),
+                                  (kb | kk) != 0 ? 1u : 0u);
+                    umma_commit(&sh->empty[s]);
+                    last_bar = &sh->empty[s];
+                    last_par = ph;
+                    if (++s == kLhStages) { s = 0; ph ^= 1u; }
+                }
+                if (stop) break;
+                umma_commit(&sh->tfull[b]);
+            }
+            if (*abort && last_bar)  // the MMAs already issued finish before TMEM is freed
+                mbar_wait(last_bar, last_par, abort, 100000000ull);
+        }
+    } else {
+        // ---- epilogue: warps 2..5, each on its quarter of the TMEM lanes
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const bool vec = (V % 8) == 0;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, it++) {
+            const int b = it & 1;
+            const uint32_t use = (uint32_t)(it >> 1);
+            if (!mbar_wait(&sh->tfull[b], use & 1u, abort)) break;
+            tc_fence_after();
+            const int n0 = tile * kLhN;
+#pragma unroll 1
+            for (int c = 0; c < kLhN / 32; c++) {
+                uint32_t r[32];
+                tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kLhN + c * 32), r);
+                const int col = n0 + c * 32;
+                if (row < B && col < V) {
+                    __nv_bfloat16* dst = out + (size_t)row * V + col;
+                    if (vec && col + 32 <= V) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]),
+                                                                          __uint_as_float(r[2 * j + 1]));
+                            pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+                        }
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            d4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                    } else {
+                        for (int j = 0; j < 32 && col + j < V; j++)
+                            dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh->tempty[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kLhTmemCols)
+                     : "memory");
+    }
+    if (threadIdx.x == 0 && *abort) atomicExch(err, 1);
+}
+
+// Restates rms_norm_kernel (qwen_model.cuh:125-177) for one row per CTA.
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ w,
+                    __nv_bfloat16* __restrict__ Y, int D, float inv_d, float eps) {
+    const int t = threadIdx.x;
+    const int half = D / 2;
+    const __nv_bfloat162* in = reinterpret_cast<const __nv_bfloat162*>(X + (size_t)blockIdx.x * D);
+    const __nv_bfloat162* wt = reinterpret_cast<const __nv_bfloat162*>(w);
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(Y + (size_t)blockIdx.x * D);
+    float lsum = 0.0f;
+    for (int i = t; i < half; i += kNormThreads) {
+        const float2 v = __bfloat1622float2(in[i]);
+        lsum = __fmaf_rn(v.x, v.x, lsum);
+        lsum = __fmaf_rn(v.y, v.y, lsum);
+    }
+    using BlockReduce = cub::BlockReduce<float, kNormThreads>;
+    __shared__ typename BlockReduce::TempStorage tmp;
+    const float total = BlockReduce(tmp).Sum(lsum);
+    __shared__ float mul;
+    if (t == 0) mul = rsqrtf(__fmaf_rn(total, inv_d, eps));
+    __syncthreads();
+    const float m = mul;
+    for (int i = t; i < half; i += kNormThreads) {
+        float2 v = __bfloat1622float2(in[i]);
+        const float2 g = wt ? __bfloat1622float2(wt[i]) : make_float2(1.0f, 1.0f);
+        v.x = __fmul_rn(__fmul_rn(v.x, m), g.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, m), g.y);
+        o[i] = __float22bfloat162_rn(v);
+    }
+}
+
+// ------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// A [rows, K] bf16 row-major matrix as 128B-swizzled [box_rows x 64] tiles.
+static bool make_map(CUtensorMap* m, const void* ptr, int rows, int K, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kLhK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// logits[B, V] = bf16(normed[B, K] . W[V, K]^T); B <= 128, K % 64 == 0.
+// Returns cudaErrorInvalidValue when a tensor map cannot be built.
+cudaError_t launch_lm_head(const __nv_bfloat16* normed, const __nv_bfloat16* W, __nv_bfloat16* logits,
+                           int B, int V, int K, int num_sms, int* err, cudaStream_t stream) {
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, normed, B, K, kLhM) || !make_map(&mb, W, V, K, kLhN)) return cudaErrorInvalidValue;
+    const int ntiles = (V + kLhN - 1) / kLhN;
+    const int grid = ntiles < num_sms ? ntiles : num_sms;
+    const size_t smem = lm_head_smem();
+    cudaError_t e = cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    lm_head_kernel<<<grid, kLhThreads, smem, stream>>>(ma, mb, logits, B, V, K, ntiles, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int B, int D,
+                           cudaStream_t stream) {
+    rmsnorm_rows_kernel<<<B, kNormThreads, 0, stream>>>(x, w, y, D, 1.0f / (float)D, 1e-6f);
+    return cudaGetLastError();
+}
+
+}  // namespace qs

@@ -206,6 +206,38 @@ class Sampler:
         return res
 
     # -- kernel timing (for benchmarks)
+    def lm_head_sample(self, hidden, weight, norm_weight=None, out=None, *, flags: int = 0,
+                       stream=None):
+        """Final RMSNorm + lm_head + stateful sample() for the rows of
+        ``hidden`` (bf16 [B, hidden_dim] device tensor; ``weight`` bf16
+        [vocab, hidden_dim]); returns int32 tokens [B] on the device."""
+        torch = _torch()
+        h = hidden if hidden.dim() == 2 else hidden.view(1, -1)
+        for t in (h, weight) + ((norm_weight,) if norm_weight is not None else ()):
+            if not t.is_cuda or not t.is_contiguous() or t.dtype != torch.bfloat16:
+                raise SamplerError(_lib.QS_ERR_INVALID, "hidden, weight and norm_weight must be "
+                                   "contiguous bf16 CUDA tensors")
+        B = int(h.shape[0])
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=h.device)
+        check(_lib.lib.qs_lm_head_sample(self._h, _ptr(h), _ptr(norm_weight), _ptr(weight), B,
+                                         int(h.shape[1]), _ptr(out), _stream_handle(stream),
+                                         int(flags)))
+        return out
+
+    def lm_head_logits(self, batch: int):
+        """The bf16 logits [batch, vocab] the last lm_head_sample produced (a
+        view of the handle's workspace)."""
+        torch = _torch()
+        p = C.c_void_p()
+        check(_lib.lib.qs_lm_head_logits(self._h, C.byref(p)))
+        if not p.value:
+            raise SamplerError(_lib.QS_ERR_INVALID, "no lm_head call yet")
+        return _wrap_device(p.value, (int(batch), self.vocab), torch.bfloat16, self.device)
+
+    def lm_head_status(self, stream=None) -> None:
+        check(_lib.lib.qs_lm_head_status(self._h, _stream_handle(stream)))
+
     def profile(self, on: bool = True) -> None:
         check(_lib.lib.qs_profile_enable(self._h, 1 if on else 0))
 
@@ -231,6 +263,39 @@ class Sampler:
             self.free()
         except Exception:
             pass
+
+
+def _wrap_device(ptr: int, shape, dtype, device: int):
+    """A torch tensor over device memory the library owns (no copy)."""
+    torch = _torch()
+    n = 1
+    for d in shape:
+        n *= int(d)
+    itemsize = torch.empty((), dtype=dtype).element_size()
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": (n * itemsize,), "typestr": "|u1",
+                                    "data": (int(ptr), False), "version": 3}
+    with torch.cuda.device(device):
+        raw = torch.as_tensor(_Mem(), device=f"cuda:{device}")
+    return raw.view(dtype).view(*shape)
+
+
+def lm_head(hidden, weight, norm_weight=None, *, stream=None):
+    """Final RMSNorm + lm_head (qwen_model.cuh:710-723) for bf16 device
+    tensors; returns (normed [B, hidden_dim], logits [B, vocab]) bf16."""
+    torch = _torch()
+    h = hidden if hidden.dim() == 2 else hidden.view(1, -1)
+    B, D = int(h.shape[0]), int(h.shape[1])
+    Vv = int(weight.shape[0])
+    normed = torch.empty((B, D), dtype=torch.bfloat16, device=h.device)
+    logits = torch.empty((B, Vv), dtype=torch.bfloat16, device=h.device)
+    err = torch.zeros(1, dtype=torch.int32, device=h.device)
+    check(_lib.lib.qs_lm_head(_ptr(h), _ptr(norm_weight), _ptr(weight), B, D, Vv, _ptr(normed),
+                              _ptr(logits), _ptr(err), _stream_handle(stream)))
+    if int(err.item()) != 0:
+        raise SamplerError(_lib.QS_ERR_CUDA, "lm_head kernel gave up waiting on its pipeline")
+    return normed, logits
 
 
 def decode_debug(dbg) -> Dict[str, np.ndarray]:
