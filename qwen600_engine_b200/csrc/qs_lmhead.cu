@@ -11,9 +11,9 @@
 // (qwen_model.cuh:607-629: bf16 inputs and output, fp32 compute).  It is a
 // persistent, warp-specialised tcgen05 GEMM:
 //   warp 0  one thread issues TMA loads (128B-swizzled K-major tiles of the
-//           normed hidden rows and of 256 vocabulary rows of W) into a
-//           4-stage shared-memory ring;
-//   warp 1  one thread issues tcgen05.mma (M = 128 batch rows, N = 256
+//           normed hidden rows and of 208 vocabulary rows of W) into a
+//           5-stage shared-memory ring;
+//   warp 1  one thread issues tcgen05.mma (M = 128 batch rows, N = 208
 //           vocabulary rows, K = 16 per instruction) into one of two TMEM
 //           accumulators, and tcgen05.commit frees each stage and hands
 //           a finished accumulator to the epilogue;
@@ -24,6 +24,7 @@
 // Every wait is bounded: after kLhWaitNs the kernel raises an error flag,
 // lets the copies and MMAs it issued finish, frees its TMEM and returns.
 #include <cuda.h>
+#include <string.h>
 #include <cudaTypedefs.h>
 
 #include <cub/block/block_reduce.cuh>
@@ -33,17 +34,21 @@
 namespace qs {
 
 constexpr int kLhM = 128;                       // batch rows per launch (MMA M)
-constexpr int kLhN = 256;                       // vocabulary rows per tile (MMA N)
+constexpr int kLhN = 208;                       // vocabulary rows per tile (MMA N): 731 tiles of
+                                                // Qwen3's 151,936 rows spread over 148 SMs
+                                                // within 1.2% of evenly
 constexpr int kLhK = 64;                        // K per stage: one 128-byte swizzle row
 constexpr int kLhStages = 4;
+constexpr uint32_t kLhOutTile = 32 * kLhN * 2;   // one epilogue warp's bf16 rows of a tile
 constexpr int kLhThreads = 192;
 constexpr uint32_t kLhStageA = kLhM * kLhK * 2;  // 16 KB
-constexpr uint32_t kLhStageB = kLhN * kLhK * 2;  // 32 KB
-constexpr uint32_t kLhTmemCols = 2 * kLhN;       // two fp32 accumulators
+constexpr uint32_t kLhStageB = kLhN * kLhK * 2;  // 26 KB
+constexpr uint32_t kLhAccStride = 256;           // TMEM columns between the two accumulators
+constexpr uint32_t kLhTmemCols = 2 * kLhAccStride;
 constexpr unsigned long long kLhWaitNs = 2000000000ull;
 
 // tcgen05.mma kind::f16 instruction descriptor: fp32 accumulator, bf16 A and
-// B, both K-major, N = 256, M = 128.
+// B, both K-major, N = kLhN, M = 128.
 constexpr uint32_t kLhIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kLhN >> 3) << 17) |
                               ((uint32_t)(kLhM >> 4) << 24);
 
@@ -56,7 +61,9 @@ struct LhShared {
     int abort;
 };
 
-size_t lm_head_smem() { return 1024 + kLhStages * (size_t)(kLhStageA + kLhStageB) + sizeof(LhShared); }
+size_t lm_head_smem() {
+    return 1024 + kLhStages * (size_t)(kLhStageA + kLhStageB) + 4 * (size_t)kLhOutTile + sizeof(LhShared);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -138,29 +145,28 @@ __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
                      smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(kLhThreads, 1)
 lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               __nv_bfloat16* __restrict__ out, int B, int V, int K, int ntiles, int* __restrict__ err) {
+               const __grid_constant__ CUtensorMap tmC, int tma_out, __nv_bfloat16* __restrict__ out, int B,
+               int V, int K, int ntiles, int* __restrict__ err) {
     extern __shared__ unsigned char lh_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(lh_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char* sA = base;                              // [stages][128 x 64 bf16]
-    unsigned char* sB = base + kLhStages * kLhStageA;      // [stages][256 x 64 bf16]
-    LhShared* sh = reinterpret_cast<LhShared*>(sB + kLhStages * kLhStageB);
+    unsigned char* sB = base + kLhStages * kLhStageA;      // [stages][kLhN x 64 bf16]
+    unsigned char* sC = sB + kLhStages * kLhStageB;          // [4 warps][32 x kLhN bf16]
+    LhShared* sh = reinterpret_cast<LhShared*>(sC + 4 * kLhOutTile);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = K / kLhK;
 
@@ -229,7 +235,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const uint32_t use = (uint32_t)(it >> 1);
                 if (!mbar_wait(&sh->tempty[b], (use & 1u) ^ 1u, abort)) break;
                 tc_fence_after();
-                const uint32_t dt = tbase + (uint32_t)(b * kLhN);
+                const uint32_t dt = tbase + (uint32_t)b * kLhAccStride;
                 for (int kb = 0; kb < nk; kb++) {
                     if (!mbar_wait(&sh->full[s], ph, abort)) { stop = true; break; }
                     tc_fence_after();
@@ -252,9 +258,14 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else {
         // ---- epilogue: warps 2..5, each on its quarter of the TMEM lanes
+        // (32 batch rows).  With tma_out the warp stages its rows of the tile
+        // in shared memory and one lane stores them with a TMA bulk tensor
+        // copy (whole 416-byte row segments; rows past B and columns past V
+        // are clipped by the copy); otherwise each lane stores its own row.
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const bool vec = (V % 8) == 0;
+        __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(sC + q * kLhOutTile) + lane * kLhN;
         int it = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, it++) {
             const int b = it & 1;
@@ -262,35 +273,56 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (!mbar_wait(&sh->tfull[b], use & 1u, abort)) break;
             tc_fence_after();
             const int n0 = tile * kLhN;
+            if (tma_out && lane == 0)  // the previous tile's store has read the staging rows
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            __syncwarp();
 #pragma unroll 1
-            for (int c = 0; c < kLhN / 32; c++) {
-                uint32_t r[32];
-                tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kLhN + c * 32), r);
-                const int col = n0 + c * 32;
+            for (int c = 0; c < kLhN / 16; c++) {
+                uint32_t r[16];
+                tmem_ld16(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)b * kLhAccStride + (uint32_t)(c * 16), r);
+                uint32_t pk[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]),
+                                                                  __uint_as_float(r[2 * j + 1]));
+                    pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                if (tma_out) {
+                    uint4* d4 = reinterpret_cast<uint4*>(stage + c * 16);
+                    d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    continue;
+                }
+                const int col = n0 + c * 16;
                 if (row < B && col < V) {
                     __nv_bfloat16* dst = out + (size_t)row * V + col;
-                    if (vec && col + 32 <= V) {
-                        uint32_t pk[16];
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]),
-                                                                          __uint_as_float(r[2 * j + 1]));
-                            pk[j] = *reinterpret_cast<const uint32_t*>(&h);
-                        }
+                    if (vec && col + 16 <= V) {
                         uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            d4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                        d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                     } else {
-                        for (int j = 0; j < 32 && col + j < V; j++)
+                        for (int j = 0; j < 16 && col + j < V; j++)
                             dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
                     }
                 }
             }
             tc_fence_before();
+            if (tma_out) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sh->tempty[b]);
+            if (lane == 0) {
+                mbar_arrive(&sh->tempty[b]);
+                if (tma_out) {
+                    asm volatile(
+                        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                            (unsigned long long)&tmC),
+                        "r"(n0), "r"(q * 32), "r"(smem_u32(sC + q * kLhOutTile))
+                        : "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+            }
         }
+        if (tma_out && lane == 0)  // the last stores complete before the CTA leaves
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -367,12 +399,27 @@ cudaError_t launch_lm_head(const __nv_bfloat16* normed, const __nv_bfloat16* W, 
                            int B, int V, int K, int num_sms, int* err, cudaStream_t stream) {
     CUtensorMap ma, mb;
     if (!make_map(&ma, normed, B, K, kLhM) || !make_map(&mb, W, V, K, kLhN)) return cudaErrorInvalidValue;
+    // the logits as [B, V] with 32-row x kLhN-column boxes, unswizzled (row
+    // pitch V * 2 bytes must be a multiple of 16)
+    CUtensorMap mc;
+    memset(&mc, 0, sizeof(mc));
+    int tma_out = 0;
+    if ((V % 8) == 0 && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0)) {
+        auto fn = encode_fn();
+        const cuuint64_t dims[2] = {(cuuint64_t)V, (cuuint64_t)B};
+        const cuuint64_t strides[1] = {(cuuint64_t)V * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)kLhN, 32};
+        const cuuint32_t estr[2] = {1, 1};
+        tma_out = fn && fn(&mc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, logits, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
     const int ntiles = (V + kLhN - 1) / kLhN;
     const int grid = ntiles < num_sms ? ntiles : num_sms;
     const size_t smem = lm_head_smem();
     cudaError_t e = cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    lm_head_kernel<<<grid, kLhThreads, smem, stream>>>(ma, mb, logits, B, V, K, ntiles, err);
+    lm_head_kernel<<<grid, kLhThreads, smem, stream>>>(ma, mb, mc, tma_out, logits, B, V, K, ntiles, err);
     return cudaGetLastError();
 }
 
