@@ -206,6 +206,60 @@ def run_reference_arm(args):
     return 0
 
 
+def measure_lm_head(torch, dev, B=128, K=1024, iters=20):
+    """RMSNorm + lm_head (qs_lm_head) at configuration 5, and the same plus
+    sampling (qs_lm_head_sample with history): CUDA events over `iters`
+    launches alternating two W copies (622 MB, larger than L2)."""
+    from qwen600_engine_b200 import _lib
+    from qwen600_engine_b200.sampler import Sampler
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    h = torch.randn((B, K), generator=g, device=dev).to(torch.bfloat16)
+    ws = [(0.02 * torch.randn((V, K), generator=g, device=dev)).to(torch.bfloat16) for _ in range(2)]
+    normed = torch.empty((B, K), dtype=torch.bfloat16, device=dev)
+    logits = torch.empty((B, V), dtype=torch.bfloat16, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream()
+
+    def one(i):
+        _lib.check(_lib.lib.qs_lm_head(h.data_ptr(), None, ws[i % 2].data_ptr(), B, K, V,
+                                       normed.data_ptr(), logits.data_ptr(), err.data_ptr(),
+                                       st.cuda_stream))
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for i in range(iters):
+        one(i)
+    b.record(st)
+    torch.cuda.synchronize()
+    us = 1e3 * a.elapsed_time(b) / iters
+    s = Sampler(0.6, 0.95, 0.05, 20, 1.1, 0.0, 0.0, 64, 1, max_batch=B, device=dev.index or 0)
+    for i in range(3):
+        s.lm_head_sample(h, ws[i % 2])
+    torch.cuda.synchronize()
+    a.record(st)
+    for i in range(iters):
+        s.lm_head_sample(h, ws[i % 2])
+    b.record(st)
+    torch.cuda.synchronize()
+    us_s = 1e3 * a.elapsed_time(b) / iters
+    s.lm_head_status()
+    s.free()
+    hbm, kind = peaks()
+    byts = V * K * 2 + B * V * 2 + 2 * B * K * 2
+    flops = 2.0 * B * K * V
+    return {"config": f"hidden [{B},{K}] bf16 -> RMSNorm -> W [{V},{K}] bf16 (random N(0,0.02^2)), fp32 accumulate, bf16 logits",
+            "us_per_launch": us, "achieved_GBps": byts / (us * 1e-6) / 1e9, "peak_GBps": hbm,
+            "frac": byts / (us * 1e-6) / 1e9 / hbm, "algorithmic_bytes": byts,
+            "tflops": flops / (us * 1e-6) / 1e12, "error_flag": int(err.item()),
+            "with_sampling_us": us_s, "sampling_rows_per_s": B / (us_s * 1e-6),
+            "note": "random weights give flat logits (std 0.64): every row takes the dense softmax "
+                    "path and ~16% of rows the tie-order pass"}
+
+
 def make_inputs(torch, B, seed, device):
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -229,6 +283,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-lm-head", dest="lm_head", action="store_false",
+                    help="skip the RMSNorm + lm_head measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -373,6 +429,12 @@ def main():
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(B * 4),
                "steps": args.e2e_steps, "path": "pinned host -> qs_sample_rows (C ABI) -> host"}
 
+    # ---- the decode tail (final RMSNorm + lm_head, SURVEY configuration 5):
+    # 128 hidden rows x W [151936, 1024] bf16, two weight copies used in turn
+    lmh = None
+    if rank == 0 and world == 1 and args.lm_head:
+        lmh = measure_lm_head(torch, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -402,6 +464,7 @@ def main():
                      "step_hbm_frac": world * B * STEP_ROW_BYTES / (ms_step / 1e3) / 1e9 / hbm / world},
         "kernel_ms_per_step": {k: pr[k] / args.steps for k in ("penalty_ms", "row_ms", "ties_ms", "emit_ms")},
         "cpu_baseline": cpu,
+        "lm_head": lmh,
         "clocks": clk.summary(),
         "gpu_launches": launches,
     }

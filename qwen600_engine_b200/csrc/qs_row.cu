@@ -678,24 +678,63 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                 float v[EPL];
                 rv.widen(hot[h], lane, f[u], r[u], v);
                 const float thr = hthr[h];
-                Tf tf = tf_identity();
+                // Usually every addition rounds to the nearest grid point
+                // regardless of the running sum's parity (no term is an exact
+                // half-unit), so the segment adds the sum of the rounded
+                // increments.  A term within the expf error band of a
+                // half-unit is formed exactly; an exact half-unit sends the
+                // segment to the parity-aware composition.
+                const bool pow2 = (23 - E) >= -126 && (23 - E) <= 127;
+                const float scale = pow2 ? exp2f((float)(23 - E)) : 0.0f;
+                uint32_t inc = 0;
+                bool ok = true, tie = false;
 #pragma unroll
                 for (int e = 0; e < EPL; e++) {
                     const float t = __fmul_rn(v[e], inv);
                     if (t >= thr) {
                         const float d = __fsub_rn(t, M);
-                        tf = tf_compose(tf, tf_element(grid_term(d, expf(d), E, fx), E));
+                        float term = expf(d);
+                        float x = pow2 ? __fmul_rn(term, scale) : ldexpf(term, 23 - E);
+                        float fr = __fsub_rn(x, floorf(x));
+                        if (!(x < 16777216.0f) || fabsf(__fsub_rn(fr, 0.5f)) <= __fmul_rn(x, 4.8e-7f)) {
+                            term = exact_exp(d, fx);
+                            x = pow2 ? __fmul_rn(term, scale) : ldexpf(term, 23 - E);
+                            fr = __fsub_rn(x, floorf(x));
+                        }
+                        if (!(x < 16777216.0f)) ok = false;
+                        else if (fr == 0.5f) tie = true;
+                        else inc += (uint32_t)rintf(x);
                     }
                 }
-                // ordered reduction: lane 0 ends with the whole segment
+                if (inc > (1u << 25)) ok = false;
+                Tf tf;
+                if (!__any_sync(0xffffffffu, tie)) {
+                    const uint32_t tot = __reduce_add_sync(0xffffffffu, ok ? inc : 0u);
+                    const bool all_ok = __all_sync(0xffffffffu, ok) && tot < (1u << 25);
+                    tf.inc0 = tot;
+                    tf.inc1 = tot;
+                    tf.out = (tot & 1u) | (((tot + 1u) & 1u) << 1);
+                    tf.ok = all_ok ? 1u : 0u;
+                } else {
+                    tf = tf_identity();
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    Tf b;
-                    b.inc0 = __shfl_down_sync(0xffffffffu, tf.inc0, o);
-                    b.inc1 = __shfl_down_sync(0xffffffffu, tf.inc1, o);
-                    b.out = __shfl_down_sync(0xffffffffu, tf.out, o);
-                    b.ok = __shfl_down_sync(0xffffffffu, tf.ok, o);
-                    if ((lane & (2 * o - 1)) == 0) tf = tf_compose(tf, b);
+                    for (int e = 0; e < EPL; e++) {
+                        const float t = __fmul_rn(v[e], inv);
+                        if (t >= thr) {
+                            const float d = __fsub_rn(t, M);
+                            tf = tf_compose(tf, tf_element(grid_term(d, expf(d), E, fx), E));
+                        }
+                    }
+                    // ordered reduction: lane 0 ends with the whole segment
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        Tf b;
+                        b.inc0 = __shfl_down_sync(0xffffffffu, tf.inc0, o);
+                        b.inc1 = __shfl_down_sync(0xffffffffu, tf.inc1, o);
+                        b.out = __shfl_down_sync(0xffffffffu, tf.out, o);
+                        b.ok = __shfl_down_sync(0xffffffffu, tf.ok, o);
+                        if ((lane & (2 * o - 1)) == 0) tf = tf_compose(tf, b);
+                    }
                 }
                 if (lane == 0) htf[h] = tf;
             }
@@ -1165,6 +1204,7 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
             rmax = fmaxf(rmax, tmax);
             if (tmax >= th) want |= 1u << u;
         }
+        if (*(volatile int*)&sh.ovf) want = 0;  // the dense method takes over; stop stashing
         while (want) {
             const int u = __ffs(want) - 1;
             want &= want - 1;
