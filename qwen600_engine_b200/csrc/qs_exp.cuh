@@ -50,8 +50,17 @@ static __device__ __noinline__ float ref_expf_fix(float x, float m, const ExpFix
     return m;
 }
 
+// The filter test is inline (one load that independent evaluations overlap);
+// only inputs the filter flags take the out-of-line table search.
 static __device__ __forceinline__ float ref_expf(float x, const ExpFix& fx) {
-    return ref_expf_fix(x, qs_exp_rn(x), fx);
+    const float m = qs_exp_rn(x);
+    uint32_t a = __float_as_uint(x);
+    if (!(a & 0x80000000u)) return m;
+    a &= 0x7FFFFFFFu;
+    if ((a >> 16) >= fx.nb) return m;
+    const uint32_t h = exp_fix_hash(a);
+    if (!((__ldg(fx.bloom + (h >> 5)) >> (h & 31)) & 1u)) return m;
+    return ref_expf_fix(x, m, fx);
 }
 
 // One ulp of a finite non-negative float (distance to the next float up).

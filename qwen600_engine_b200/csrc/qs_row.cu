@@ -444,14 +444,14 @@ __device__ __noinline__ float serial_sum(const float* a, int n, float s) {
     return s;
 }
 
-// Replays hot segment g element by element from running sum s (warp-wide;
-// returns the new sum).  Each lane first forms the exact terms of its EPL
-// elements; additions that keep the sum inside its binade are then composed
-// with a warp scan, and the lane whose terms leave the binade adds them one at
-// a time before the scan resumes after it.
+// Adds hot segment g's terms to running sum s in index order (warp-wide;
+// returns the new sum): the lanes form the reference's exact terms in
+// parallel into `buf` (>= 32 * EPL floats of shared memory), then one lane
+// adds them sequentially.  Used where the sum crosses a binade inside the
+// segment (a serial chain of fp32 additions beats a scan per crossing).
 template <typename T>
 __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float thr, float inv, float M,
-                                           float s, const ExpFix& fx) {
+                                           float s, float* buf, const ExpFix& fx) {
     constexpr int EPL = RowView<T>::EPL;
     const int lane = threadIdx.x & 31;
     float v[EPL];
@@ -462,31 +462,13 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
         const float t = __fmul_rn(v[e], inv);
         ex[e] = (t >= thr) ? ref_expf(__fsub_rn(t, M), fx) : 0.0f;
     }
-    int start = 0;  // lanes below `start` are already added
-    while (start < 32) {
-        const int E = sum_binade(s);
-        const uint32_t S = sum_units(s, E);
-        Tf f = tf_identity();
-        if (lane >= start) {
 #pragma unroll
-            for (int e = 0; e < EPL; e++) f = tf_compose(f, tf_element(ex[e], E));
-        }
-        const Tf pre = warp_scan_tf(f);
-        const uint32_t inc = (S & 1u) ? pre.inc1 : pre.inc0;
-        const bool bad = (lane >= start) && (!pre.ok || S + inc >= kTwo24);
-        const unsigned bm = __ballot_sync(0xffffffffu, bad);
-        if (!bm) {
-            const uint32_t tot = __shfl_sync(0xffffffffu, inc, 31);
-            s = ldexpf((float)(S + tot), E - 23);
-            break;
-        }
-        const int c = __ffs(bm) - 1;
-        const uint32_t prev = __shfl_sync(0xffffffffu, inc, c > 0 ? c - 1 : 0);
-        s = ldexpf((float)(S + ((c > start) ? prev : 0u)), E - 23);
-#pragma unroll
-        for (int e = 0; e < EPL; e++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, ex[e], c));
-        start = c + 1;
-    }
+    for (int e = 0; e < EPL; e += 4)
+        *reinterpret_cast<float4*>(buf + lane * EPL + e) = make_float4(ex[e], ex[e + 1], ex[e + 2], ex[e + 3]);
+    __syncwarp();
+    if (lane == 0) s = serial_sum(buf, 32 * EPL, s);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    __syncwarp();
     return s;
 }
 
@@ -538,7 +520,7 @@ struct RowShared {
 // sum in sh->sum.  segm holds the segment maxima of t.
 template <typename T>
 __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* segm, float inv, float M,
-                                       unsigned char* region, RowShared* sh, ExpFix fx) {
+                                       unsigned char* region, float* wbuf, RowShared* sh, ExpFix fx) {
     constexpr int EPL = RowView<T>::EPL;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int* hot = (int*)region;                          // hot segment ids, in order
@@ -770,7 +752,7 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                 h += nok;
             }
             if (nok < 32 && h < nhot) {
-                s = walk_segment<T>(rv, hot[h], hthr[h], inv, M, s, fx);
+                s = walk_segment<T>(rv, hot[h], hthr[h], inv, M, s, wbuf, fx);
                 fb++;
                 h++;
             }
@@ -1330,7 +1312,7 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
         stamp(5);
         if (tid == 0) { sh.sum = serial_sum(slist, nst, 0.0f); sh.fb = -nst; }
     } else {
-        dense_sum<T>(rv, nseg, segm, inv, M, region, &sh, fx);
+        dense_sum<T>(rv, nseg, segm, inv, M, region, cd.ct, &sh, fx);
     }
     __syncthreads();
     const float sum = sh.sum;
