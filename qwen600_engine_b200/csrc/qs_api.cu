@@ -20,21 +20,18 @@
 namespace qs {
 
 template <typename T>
-cudaError_t launch_penalty(const T*, int, int, const int*, int, const int*, const float*,
-                          const float*, float, float, float, int*, int*, float*, int, float*,
-                          cudaStream_t);
-
-template <typename T>
-cudaError_t launch_row_kernel(const T*, int, int, RowParams, const int*, const int*, const float*,
-                              int, unsigned long long*, RowResult*, int*, int*, int*, float*, int,
-                              ExpFix, cudaStream_t, long long* phase_cycles = nullptr);
+cudaError_t launch_row_kernel(const T*, int, int, RowParams, RowWindow, unsigned long long*,
+                              RowResult*, int*, int*, int*, float*, int, ExpFix, cudaStream_t,
+                              long long* phase_cycles = nullptr);
+cudaError_t launch_write_penalized(float*, int, int, const int*, const int*, const float*, int,
+                                   cudaStream_t);
 template <typename T>
 cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
                                const int*, const int*, RowResult*, unsigned long long*, int*, int,
                                int*, float*, int, ExpFix, cudaStream_t,
                                long long* phase_cycles = nullptr);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
-                        float*, cudaStream_t);
+                        float*, float*, cudaStream_t);
 template <typename T>
 cudaError_t launch_probs(const T*, int, int, const int*, const int*, const float*, int,
                          const RowResult*, float*, ExpFix, cudaStream_t);
@@ -94,6 +91,7 @@ struct qs_sampler {
     int* hcount = nullptr;
     int* hpos = nullptr;
     float* token_counts = nullptr;
+    float* slot_counts = nullptr;  // [B, window]: token_counts of each ring slot's token
     unsigned long long* rng = nullptr;
     // host-entry staging
     float* d_in = nullptr;
@@ -170,7 +168,7 @@ static void release(qs_sampler* s) {
     cudaGetDevice(&prev);
     cudaSetDevice(s->device);
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
-                    s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts,
+                    s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts, s->slot_counts,
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
                     s->lh_normed, s->lh_logits, s->lh_err};
     for (void* p : ptrs)
@@ -274,6 +272,7 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
         ALLOC(s->hcount, sizeof(int) * B);
         ALLOC(s->hpos, sizeof(int) * B);
         ALLOC(s->token_counts, sizeof(float) * B * V);
+        ALLOC(s->slot_counts, sizeof(float) * B * W);
     }
 #undef ALLOC
     cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
@@ -297,6 +296,7 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
         e = cudaMemset(s->hcount, 0, sizeof(int) * B);
         if (e == cudaSuccess) e = cudaMemset(s->hpos, 0, sizeof(int) * B);
         if (e == cudaSuccess) e = cudaMemset(s->token_counts, 0, sizeof(float) * B * V);
+        if (e == cudaSuccess) e = cudaMemset(s->slot_counts, 0, sizeof(float) * B * W);
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -364,6 +364,7 @@ int qs_reset_sampler_history(qs_sampler* s) {
     CK(cudaMemsetAsync(s->hcount, 0, sizeof(int) * B, s->stream));
     CK(cudaMemsetAsync(s->hpos, 0, sizeof(int) * B, s->stream));
     CK(cudaMemsetAsync(s->token_counts, 0, sizeof(float) * B * s->vocab, s->stream));
+    CK(cudaMemsetAsync(s->slot_counts, 0, sizeof(float) * B * s->window, s->stream));
     CK(cudaStreamSynchronize(s->stream));
     return QS_OK;
 }
@@ -379,7 +380,6 @@ struct Call {
     int hist_stride;
     const int* hist_count;
     const float* slot_counts;
-    const float* dense_counts;
     unsigned long long* rng;
     int* tokens;
     qs_row_debug* dbg;
@@ -390,7 +390,8 @@ struct Call {
     int* ring;
     int* hcount;
     int* hpos;
-    float* token_counts;  // history update target (stateful)
+    float* token_counts;  // history update targets (stateful)
+    float* ring_counts;
     cudaStream_t stream;
     unsigned flags;
 };
@@ -416,22 +417,15 @@ static int run(qs_sampler* s, const Call& c) {
                             p.presence_penalty != 0.0f);
     s->prof.calls++;
     if (s->profiling) s->prof.timed_calls++;
+    // the row kernel applies the window's penalties (sampler.h:114-141) to the
+    // raw logits as it streams them and leaves the override tables for the
+    // later passes
+    RowWindow win{};
     if (penalties) {
-        KernelScope ks(s, 0, c.stream);
-        float* wb = (c.flags & QS_FLAG_WRITE_PENALIZED) ? (float*)c.logits : nullptr;
-        if (c.dtype == QS_F32) {
-            CK(launch_penalty<float>((const float*)c.logits, B, V, c.hist, c.hist_stride,
-                                     c.hist_count, c.slot_counts, c.dense_counts,
-                                     p.repetition_penalty, p.frequency_penalty, p.presence_penalty,
-                                     s->ov_n, s->ov_idx, s->ov_val, s->ov_stride, wb, c.stream));
-        } else {
-            CK(launch_penalty<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, c.hist,
-                                             c.hist_stride, c.hist_count, c.slot_counts,
-                                             c.dense_counts, p.repetition_penalty,
-                                             p.frequency_penalty, p.presence_penalty, s->ov_n,
-                                             s->ov_idx, s->ov_val, s->ov_stride, nullptr,
-                                             c.stream));
-        }
+        win.hist = c.hist; win.count = c.hist_count; win.slot_counts = c.slot_counts;
+        win.window = c.hist_stride;
+        win.rp = p.repetition_penalty; win.fp = p.frequency_penalty; win.pp = p.presence_penalty;
+        win.ov_n = s->ov_n; win.ov_idx = s->ov_idx; win.ov_val = s->ov_val; win.ov_stride = s->ov_stride;
     }
     const int* ovn = penalties ? s->ov_n : nullptr;
     CK(cudaMemsetAsync(s->slow_count, 0, sizeof(int), c.stream));
@@ -439,14 +433,13 @@ static int run(qs_sampler* s, const Call& c) {
     {
     KernelScope ks(s, 1, c.stream);
     if (c.dtype == QS_F32) {
-        CK(launch_row_kernel<float>((const float*)c.logits, B, V, rp, ovn, s->ov_idx, s->ov_val,
-                                    s->ov_stride, c.rng, s->res, s->slow_list, s->slow_count,
-                                    c.cand_index, c.cand_prob, c.cand_cap, s->fix(), c.stream));
+        CK(launch_row_kernel<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res,
+                                    s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
+                                    c.cand_cap, s->fix(), c.stream));
     } else {
-        CK(launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, ovn,
-                                            s->ov_idx, s->ov_val, s->ov_stride, c.rng, s->res,
-                                            s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
-                                            c.cand_cap, s->fix(), c.stream));
+        CK(launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng,
+                                            s->res, s->slow_list, s->slow_count, c.cand_index,
+                                            c.cand_prob, c.cand_cap, s->fix(), c.stream));
     }
     }
     if (!greedy && topk && !(c.flags & QS_FLAG_INDEX_TIES)) {
@@ -477,7 +470,12 @@ static int run(qs_sampler* s, const Call& c) {
     {
         KernelScope ks(s, 3, c.stream);
         CK(launch_emit(B, V, s->window, s->res, c.tokens, c.dbg, c.ring, c.hcount, c.hpos,
-                       c.token_counts, c.stream));
+                       c.token_counts, c.ring_counts, c.stream));
+    }
+    if (penalties && (c.flags & QS_FLAG_WRITE_PENALIZED)) {
+        KernelScope ks(s, 4, c.stream);
+        CK(launch_write_penalized((float*)c.logits, B, V, s->ov_n, s->ov_idx, s->ov_val, s->ov_stride,
+                                  c.stream));
     }
     return QS_OK;
 }
@@ -491,9 +489,10 @@ int qs_sample(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, in
     Call c{};
     c.logits = d_logits; c.dtype = dtype; c.batch = batch; c.vocab = s->vocab;
     c.hist = s->ring; c.hist_stride = s->window; c.hist_count = s->hcount;
-    c.dense_counts = s->token_counts;
+    c.slot_counts = s->slot_counts;
     c.rng = s->rng; c.tokens = d_tokens;
     c.ring = s->ring; c.hcount = s->hcount; c.hpos = s->hpos; c.token_counts = s->token_counts;
+    c.ring_counts = s->slot_counts;
     c.stream = (cudaStream_t)stream; c.flags = flags;
     return run(s, c);
 }

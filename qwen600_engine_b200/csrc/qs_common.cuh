@@ -38,6 +38,20 @@ struct TieParams {
     int top_k;
 };
 
+// The row's penalty window and the override tables the row kernel writes
+// for the later passes (ties, probabilities, penalised write-back).
+struct RowWindow {
+    const int* hist;          // [B, window] token ids (slot order), or NULL
+    const int* count;         // [B] slots in use
+    const float* slot_counts; // [B, window] count of each slot's token, or NULL
+    int window;
+    float rp, fp, pp;
+    int* ov_n;                // [B] out: distinct in-range window tokens
+    int* ov_idx;              // [B, ov_stride] out: those tokens, ascending
+    float* ov_val;            // [B, ov_stride] out: their penalised logits
+    int ov_stride;
+};
+
 // Per-row results shared between the row kernel, the exact-tie kernel, the
 // history update and the debug readers.  Mirrors qs_row_debug's first fields.
 struct RowResult {

@@ -188,9 +188,9 @@ struct RowView {
     const T* L;
     int V;
     bool aligned;
-    const unsigned char* segov;
-    const int* ovi;
-    const float* ovv;
+    const unsigned char* segov;   // segments holding a window token
+    const int* ovi;               // window tokens, ascending
+    const float* ovv;             // their penalised logits
     int nov;
     static constexpr int EPL = Elem<T>::kPerLane;
     static constexpr int SEG = 32 * EPL;
@@ -223,7 +223,7 @@ struct RowView {
                 v[e] = (base + e < V) ? Elem<T>::widen(L[base + e]) : -INFINITY;
         }
         if (segov[g]) {
-            int lo = 0, hi = nov;  // first override >= base
+            int lo = 0, hi = nov;  // first window token >= base
             while (lo < hi) { int m = (lo + hi) >> 1; if (ovi[m] < base) lo = m + 1; else hi = m; }
 #pragma unroll
             for (int e = 0; e < EPL; e++)
@@ -474,8 +474,9 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
 
 // Shared-memory layout of one row, shared by the kernel and its launcher.
 struct RowSmem {
-    size_t segm, segk, segov, ovi, ovv, pubr, region, ct, ci, cp, so, ck, rhist, total;
-    int nseg, nrounds, scap, ccap;
+    size_t segm, segk, segov, ovi, ovv, ofirst, pairs, pcnt, pubr, region, ct, ci, cp, so, ck, rhist,
+        total;
+    int nseg, nrounds, scap, ccap, npairs;
     __host__ __device__ static size_t r16(size_t b) { return (b + 15) & ~(size_t)15; }
     __host__ __device__ RowSmem(int V, int seg, int ov_stride, int ccap_, int scap_) {
         nseg = (V + seg - 1) / seg;
@@ -487,8 +488,13 @@ struct RowSmem {
         segm = p; p += r16(4 * (size_t)nseg);
         segk = p; p += r16(4 * (size_t)nseg);
         segov = p; p += r16((size_t)nseg);
+        npairs = 1;
+        while (npairs < (int)ovs) npairs <<= 1;
         ovi = p; p += r16(4 * ovs);
         ovv = p; p += r16(4 * ovs);
+        ofirst = p; p += r16(4 * ovs);
+        pairs = p; p += r16(16 * (size_t)npairs);  // sorted pairs + a second buffer
+        pcnt = p; p += r16(4 * ovs);
         pubr = p; p += r16(4 * (size_t)nrounds);
         region = p;
         const size_t fast = 16 * (size_t)scap + 8 * (size_t)nseg;  // stash t, i, e, ordered terms; tables
@@ -1027,9 +1033,7 @@ __device__ __noinline__ void finish_by_segments(RowView<T> rv, int nseg, const f
 
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
-row_kernel(const T* __restrict__ logits, int V, RowParams prm,
-           const int* __restrict__ ov_n, const int* __restrict__ ov_idx,
-           const float* __restrict__ ov_val, int ov_stride,
+row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
            unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
            int* __restrict__ slow_list, int* __restrict__ slow_count,
            int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
@@ -1039,7 +1043,7 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
     constexpr int U = kRowRound / kRowWarps;  // segments in flight per warp in the streaming pass
     const int row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const RowSmem L(V, SEG, ov_stride, ccap, scap);
+    const RowSmem L(V, SEG, win.window, ccap, scap);
     const int nseg = L.nseg;
 
     // ---- shared memory carve-up
@@ -1049,6 +1053,9 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
     unsigned char* segov = smem + L.segov;
     int* ovi = (int*)(smem + L.ovi);
     float* ovv = (float*)(smem + L.ovv);
+    int* ofirst = (int*)(smem + L.ofirst);
+    unsigned long long* pairs = (unsigned long long*)(smem + L.pairs);
+    float* pcnt = (float*)(smem + L.pcnt);
     uint32_t* pubr = (uint32_t*)(smem + L.pubr);      // per streaming round: max key seen
     unsigned char* region = smem + L.region;          // stash, or the dense method's tables
     float* st_t = (float*)region;
@@ -1070,17 +1077,95 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm,
     const bool greedy = prm.temperature < 1e-6f;
     const float inv = greedy ? 1.0f : __fdiv_rn(1.0f, prm.temperature);
 
-    // ---- overrides, tables
-    const int nov = ov_n ? ov_n[row] : 0;
-    for (int i = tid; i < nov; i += kRowThreads) {
-        ovi[i] = ov_idx[(size_t)row * ov_stride + i];
-        ovv[i] = ov_val[(size_t)row * ov_stride + i];
-    }
+    // ---- the row's penalty window (sampler.h:114-141): slots sorted by
+    // (token, slot), distinct tokens and the slot range of each; the values
+    // are formed from the raw logits as the streaming pass reads them
+    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); sh.misc[7] = 0; }
     for (int g = tid; g < nseg; g += kRowThreads) { segov[g] = 0; scnt[g] = 0; }
     for (int j = tid; j < L.nrounds; j += kRowThreads) pubr[j] = fkey(-INFINITY);
-    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); }
-    __syncthreads();
-    for (int i = tid; i < nov; i += kRowThreads) segov[ovi[i] / SEG] = 1;
+    int cntw = (win.hist && win.count) ? win.count[row] : 0;
+    cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
+    const bool pen_on = cntw > 0 && (win.rp != 1.0f || win.fp != 0.0f || win.pp != 0.0f);
+    int nov = 0;
+    if (pen_on) {
+        int npow = 1;
+        while (npow < cntw) npow <<= 1;
+        unsigned long long* keys = pairs + npow;  // unsorted (token, slot) keys
+        for (int i = tid; i < npow; i += kRowThreads) {
+            const int t = i < cntw ? win.hist[(size_t)row * win.window + i] : -1;
+            keys[i] = (t >= 0 && t < V) ? (((unsigned long long)(unsigned)t << 32) | (unsigned)i) : ~0ull;
+            if (i < cntw) pcnt[i] = win.slot_counts ? win.slot_counts[(size_t)row * win.window + i] : 0.0f;
+        }
+        __syncthreads();
+        if (npow <= 256) {
+            // rank sort (keys differ in the slot): one pass, one barrier
+            for (int i = tid; i < npow; i += kRowThreads) {
+                const unsigned long long x = keys[i];
+                int r = 0;
+                for (int j = 0; j < npow; j++) r += keys[j] < x || (keys[j] == x && j < i);
+                pairs[r] = x;
+            }
+            __syncthreads();
+        } else {
+            for (int i = tid; i < npow; i += kRowThreads) pairs[i] = keys[i];
+            __syncthreads();
+            for (int size = 2; size <= npow; size <<= 1) {  // ascending bitonic sort
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    for (int i = tid; i < npow / 2; i += kRowThreads) {
+                        const int lo = 2 * stride * (i / stride) + (i % stride);
+                        const int hi = lo + stride;
+                        const bool up = ((lo & size) == 0);
+                        const unsigned long long x = pairs[lo], y = pairs[hi];
+                        if ((x > y) == up) { pairs[lo] = y; pairs[hi] = x; }
+                    }
+                    __syncthreads();
+                }
+            }
+        }
+        // distinct tokens: rank by an exclusive scan of "first of its token" flags
+        const int per = (npow + kRowThreads - 1) / kRowThreads;
+        const int c0 = tid * per, c1 = min(c0 + per, npow);
+        int nd = 0, nvalid = 0;
+        for (int i = c0; i < c1; i++) {
+            const bool valid = pairs[i] != ~0ull;
+            nvalid += valid;
+            nd += valid && (i == 0 || (pairs[i] >> 32) != (pairs[i - 1] >> 32));
+        }
+        if (nvalid) atomicAdd(&sh.misc[7], nvalid);
+        int tot;
+        int k = rblock_excl_scan(nd, sh.red_i, &tot);
+        for (int i = c0; i < c1; i++) {
+            if (pairs[i] != ~0ull && (i == 0 || (pairs[i] >> 32) != (pairs[i - 1] >> 32))) {
+                ovi[k] = (int)(pairs[i] >> 32);
+                ofirst[k] = i;
+                k++;
+            }
+        }
+        nov = tot;
+        __syncthreads();
+        const int nv = sh.misc[7];
+        // each window token's penalised value from its raw logit, replaying
+        // its occurrences in slot order
+        const T* Lrow = logits + (size_t)row * V;
+        for (int j = tid; j < nov; j += kRowThreads) {
+            const int t = ovi[j];
+            const int q1 = (j + 1 < nov) ? ofirst[j + 1] : nv;
+            float x = Elem<T>::widen(Lrow[t]);
+            for (int q = ofirst[j]; q < q1; q++) {
+                if (win.rp != 1.0f) x = (x > 0.0f) ? __fdiv_rn(x, win.rp) : __fmul_rn(x, win.rp);
+                if (win.fp != 0.0f)
+                    x = __fsub_rn(x, __fmul_rn(win.fp, pcnt[(int)(pairs[q] & 0xFFFFFFFFull)]));
+                if (win.pp != 0.0f) x = __fsub_rn(x, win.pp);
+            }
+            ovv[j] = x;
+            segov[t / SEG] = 1;
+            if (win.ov_idx) {
+                win.ov_idx[(size_t)row * win.ov_stride + j] = t;
+                win.ov_val[(size_t)row * win.ov_stride + j] = x;
+            }
+        }
+    }
+    if (tid == 0 && win.ov_n) win.ov_n[row] = nov;
     __syncthreads();
 
     RowView<T> rv;
@@ -1461,37 +1546,51 @@ int row_kernel_ccap(int top_k, int V) {
     return c;
 }
 
-size_t row_kernel_smem(int V, int dtype_bytes, int ov_stride, int ccap) {
-    const RowSmem L(V, 32 * (16 / dtype_bytes), ov_stride, ccap, kStashCap);
+size_t row_kernel_smem(int V, int dtype_bytes, int window, int ccap) {
+    const RowSmem L(V, 32 * (16 / dtype_bytes), window, ccap, kStashCap);
     return L.total;
 }
 
 template <typename T>
-cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, const int* ov_n,
-                              const int* ov_idx, const float* ov_val, int ov_stride,
+cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, RowWindow win,
                               unsigned long long* rng, RowResult* res, int* slow_list,
                               int* slow_count, int* cand_index, float* cand_prob, int cand_cap,
                               ExpFix fx, cudaStream_t stream, long long* phase_cycles) {
     const int ccap = row_kernel_ccap(prm.top_k, V);
-    const size_t smem = row_kernel_smem(V, (int)sizeof(T), ov_stride, ccap);
+    if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
+    const size_t smem = row_kernel_smem(V, (int)sizeof(T), win.window, ccap);
     cudaError_t err = cudaFuncSetAttribute(row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err != cudaSuccess) return err;
-    row_kernel<T><<<B, kRowThreads, smem, stream>>>(logits, V, prm, ov_n, ov_idx, ov_val, ov_stride,
-                                                    rng, res, slow_list, slow_count, cand_index,
-                                                    cand_prob, cand_cap, fx, ccap, kStashCap,
-                                                    phase_cycles);
+    row_kernel<T><<<B, kRowThreads, smem, stream>>>(logits, V, prm, win, rng, res, slow_list,
+                                                    slow_count, cand_index, cand_prob, cand_cap, fx,
+                                                    ccap, kStashCap, phase_cycles);
     return cudaGetLastError();
 }
 
-template cudaError_t launch_row_kernel<float>(const float*, int, int, RowParams, const int*,
-                                              const int*, const float*, int, unsigned long long*,
-                                              RowResult*, int*, int*, int*, float*, int, ExpFix,
-                                              cudaStream_t, long long*);
+template cudaError_t launch_row_kernel<float>(const float*, int, int, RowParams, RowWindow,
+                                              unsigned long long*, RowResult*, int*, int*, int*,
+                                              float*, int, ExpFix, cudaStream_t, long long*);
 template cudaError_t launch_row_kernel<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams,
-                                                      const int*, const int*, const float*, int,
-                                                      unsigned long long*, RowResult*, int*, int*,
-                                                      int*, float*, int, ExpFix, cudaStream_t,
-                                                      long long*);
+                                                      RowWindow, unsigned long long*, RowResult*,
+                                                      int*, int*, int*, float*, int, ExpFix,
+                                                      cudaStream_t, long long*);
+
+// QS_FLAG_WRITE_PENALIZED: the reference's in-place penalty update of fp32
+// logits (sampler.h:114-141), written after every pass has read the raw row.
+__global__ void write_penalized_kernel(float* __restrict__ logits, int V, const int* __restrict__ ov_n,
+                                       const int* __restrict__ ov_idx, const float* __restrict__ ov_val,
+                                       int ov_stride) {
+    const int row = blockIdx.x;
+    const int n = ov_n[row];
+    for (int k = threadIdx.x; k < n; k += blockDim.x)
+        logits[(size_t)row * V + ov_idx[(size_t)row * ov_stride + k]] = ov_val[(size_t)row * ov_stride + k];
+}
+
+cudaError_t launch_write_penalized(float* logits, int B, int V, const int* ov_n, const int* ov_idx,
+                                   const float* ov_val, int ov_stride, cudaStream_t stream) {
+    write_penalized_kernel<<<B, 128, 0, stream>>>(logits, V, ov_n, ov_idx, ov_val, ov_stride);
+    return cudaGetLastError();
+}
 
 }  // namespace qs

@@ -30,15 +30,11 @@
 namespace qs {
 
 template <typename T>
-cudaError_t launch_penalty(const T*, int, int, const int*, int, const int*, const float*,
-                          const float*, float, float, float, int*, int*, float*, int, float*,
-                          cudaStream_t);
-template <typename T>
-cudaError_t launch_row_kernel(const T*, int, int, RowParams, const int*, const int*, const float*,
-                              int, unsigned long long*, RowResult*, int*, int*, int*, float*, int,
-                              ExpFix, cudaStream_t, long long* phase_cycles);
+cudaError_t launch_row_kernel(const T*, int, int, RowParams, RowWindow, unsigned long long*,
+                              RowResult*, int*, int*, int*, float*, int, ExpFix, cudaStream_t,
+                              long long* phase_cycles);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
-                        float*, cudaStream_t);
+                        float*, float*, cudaStream_t);
 
 constexpr int kStaticMaxBatch = 1024;
 constexpr int kStaticMaxWindow = 128;
@@ -115,35 +111,27 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
     cudaStream_t st = (cudaStream_t)stream;
     const bool penalties = window > 0 && (repetition_penalty != 1.0f ||
                                           frequency_penalty != 0.0f || presence_penalty != 0.0f);
+    RowWindow win{};
     if (penalties) {
-        if (dtype == QS_F32)
-            e = launch_penalty<float>((const float*)d_logits, batch, vocab, d_hist, window,
-                                      d_hist_count, d_hist_counts, nullptr, repetition_penalty,
-                                      frequency_penalty, presence_penalty, sc->ov_n, sc->ov_idx,
-                                      sc->ov_val, kStaticMaxWindow, nullptr, st);
-        else
-            e = launch_penalty<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, d_hist,
-                                              window, d_hist_count, d_hist_counts, nullptr,
-                                              repetition_penalty, frequency_penalty,
-                                              presence_penalty, sc->ov_n, sc->ov_idx, sc->ov_val,
-                                              kStaticMaxWindow, nullptr, st);
-        if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "penalty kernel", cudaGetErrorString(e));
+        win.hist = d_hist; win.count = d_hist_count; win.slot_counts = d_hist_counts;
+        win.window = window;
+        win.rp = repetition_penalty; win.fp = frequency_penalty; win.pp = presence_penalty;
+        win.ov_n = sc->ov_n; win.ov_idx = sc->ov_idx; win.ov_val = sc->ov_val;
+        win.ov_stride = kStaticMaxWindow;
     }
     const RowParams rp{0.0f, 1.0f, 0.0f, 0, 0u};  // temperature 0: the argmax branch
     const ExpFix none{nullptr, nullptr, nullptr, 0u};
     if (dtype == QS_F32)
-        e = launch_row_kernel<float>((const float*)d_logits, batch, vocab, rp,
-                                     penalties ? sc->ov_n : nullptr, sc->ov_idx, sc->ov_val,
-                                     kStaticMaxWindow, sc->rng, sc->res, sc->slow_list,
-                                     sc->slow_count, nullptr, nullptr, 0, none, st, nullptr);
+        e = launch_row_kernel<float>((const float*)d_logits, batch, vocab, rp, win, sc->rng, sc->res,
+                                     sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none, st,
+                                     nullptr);
     else
-        e = launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, rp,
-                                             penalties ? sc->ov_n : nullptr, sc->ov_idx,
-                                             sc->ov_val, kStaticMaxWindow, sc->rng, sc->res,
-                                             sc->slow_list, sc->slow_count, nullptr, nullptr, 0,
-                                             none, st, nullptr);
+        e = launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, rp, win,
+                                             sc->rng, sc->res, sc->slow_list, sc->slow_count,
+                                             nullptr, nullptr, 0, none, st, nullptr);
     if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "row kernel", cudaGetErrorString(e));
-    e = launch_emit(batch, vocab, 0, sc->res, d_tokens, nullptr, nullptr, nullptr, nullptr, nullptr, st);
+    e = launch_emit(batch, vocab, 0, sc->res, d_tokens, nullptr, nullptr, nullptr, nullptr, nullptr,
+                    nullptr, st);
     if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "emit kernel", cudaGetErrorString(e));
     return QS_OK;
 }

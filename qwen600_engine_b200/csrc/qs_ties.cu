@@ -629,7 +629,7 @@ template cudaError_t launch_ties_kernel<__nv_bfloat16>(const __nv_bfloat16*, int
 // its history exactly as sampler.h:257-267 does.
 __global__ void emit_kernel(int B, int V, int W, const RowResult* __restrict__ res,
                             int* __restrict__ tokens, qs_row_debug_dev* dbg, int* ring,
-                            int* hcount, int* hpos, float* token_counts) {
+                            int* hcount, int* hpos, float* token_counts, float* ring_counts) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= B) return;
     const RowResult rr = res[r];
@@ -643,19 +643,26 @@ __global__ void emit_kernel(int B, int V, int W, const RowResult* __restrict__ r
         dbg[r] = d;
     }
     if (ring && W > 0 && rr.token >= 0 && rr.token < V) {
-        token_counts[(size_t)r * V + rr.token] += 1.0f;
+        const float c = token_counts[(size_t)r * V + rr.token] + 1.0f;
+        token_counts[(size_t)r * V + rr.token] = c;
         int p = hpos[r];
         ring[(size_t)r * W + p] = rr.token;
         hpos[r] = (p + 1) % W;
         if (hcount[r] < W) hcount[r] = hcount[r] + 1;
+        // every slot that holds the token sees its new count (the penalty
+        // pass reads counts per slot; slots past the count are rewritten
+        // before they are read)
+        if (ring_counts)
+            for (int j = 0; j < W; j++)
+                if (ring[(size_t)r * W + j] == rr.token) ring_counts[(size_t)r * W + j] = c;
     }
 }
 
 cudaError_t launch_emit(int B, int V, int W, const RowResult* res, int* tokens,
                         qs_row_debug_dev* dbg, int* ring, int* hcount, int* hpos,
-                        float* token_counts, cudaStream_t stream) {
+                        float* token_counts, float* ring_counts, cudaStream_t stream) {
     emit_kernel<<<(B + 127) / 128, 128, 0, stream>>>(B, V, W, res, tokens, dbg, ring, hcount, hpos,
-                                                      token_counts);
+                                                      token_counts, ring_counts);
     return cudaGetLastError();
 }
 
