@@ -194,6 +194,66 @@ __device__ __forceinline__ int place_stops(const Arr& A, int c0, int c1, const P
     return nswap;
 }
 
+// Global-round forms: the counting pass also records each element's L / R
+// classification as one bit per element in shared memory (word w of a warp's
+// chunk covers chunk elements 32w .. 32w + 31), so the placing pass reads
+// bits from shared memory instead of keys from L2.
+template <class Pred>
+__device__ __forceinline__ void count_stops_bits(const GlobalArr& A, int c0, int c1, const Pred& pv,
+                                                 unsigned* mL, unsigned* mR, int* cl, int* cr) {
+    const int lane = threadIdx.x & 31;
+    constexpr int UN = 8;
+    int l = 0, r = 0;
+    for (int q0 = c0; q0 < c1; q0 += 32 * UN) {
+        uint32_t v[UN];
+#pragma unroll
+        for (int u = 0; u < UN; u++) {
+            const int q = q0 + u * 32 + lane;
+            v[u] = (q < c1) ? A.key(q) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < UN; u++) {
+            const int q = q0 + u * 32 + lane;
+            const unsigned bl = __ballot_sync(0xffffffffu, q < c1 && pv.le(v[u]));
+            const unsigned br = __ballot_sync(0xffffffffu, q < c1 && pv.ge(v[u]));
+            if (lane == 0 && q0 + u * 32 < c1) {
+                const int w = (q0 - c0) / 32 + u;
+                mL[w] = bl;
+                mR[w] = br;
+            }
+            l += __popc(bl);
+            r += __popc(br);
+        }
+    }
+    *cl = l;
+    *cr = r;
+}
+
+template <class Pos>
+__device__ __forceinline__ int place_stops_bits(int c0, int c1, const unsigned* mL, const unsigned* mR,
+                                                int aL, int bB, int totR, const Pos& posL,
+                                                const Pos& posR) {
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    int nswap = 0;
+    const int nw = (c1 - c0 + 31) / 32;
+    for (int w = 0; w < nw; w++) {
+        const unsigned bl = mL[w], br = mR[w];
+        const int q = c0 + 32 * w + lane;
+        const bool isL = (bl >> lane) & 1u, isR = (br >> lane) & 1u;
+        const int a = aL + __popc(bl & lt) + 1;      // #L in [lo, q]
+        const int b = totR - bB - __popc(br & lt);  // #R in [q, hi]
+        if (isL) {
+            posL.st(a - 1, q);
+            nswap += (b >= a);
+        }
+        if (isR) posR.st(b - 1, q);
+        aL += __popc(bl);
+        bB += __popc(br);
+    }
+    return nswap;
+}
+
 // The scans' final (i, j) after T swaps (the serial loop's exit state).
 template <class Pos>
 __device__ __forceinline__ void final_ij(const Pos& posL, const Pos& posR, int T, int totL, int totR,
@@ -354,6 +414,65 @@ __device__ void cta_round(const Arr& A, const Pos& posL, const Pos& posR, int lo
     __syncthreads();
 }
 
+// One partition round on [lo, hi] by one warp, in shared memory (small
+// ranges: no block barriers).  Every lane returns (i, j).
+template <class Arr, class Pos, class Pred>
+__device__ void warp_round(const Arr& A, const Pos& posL, const Pos& posR, int lo, int hi,
+                           const Pred& pv, int* oi, int* oj) {
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    int totL = 0, totR = 0;
+    for (int q0 = lo; q0 <= hi; q0 += 32) {
+        const int q = q0 + lane;
+        const bool in = q <= hi;
+        const uint32_t v = in ? A.key(q) : 0u;
+        totL += __popc(__ballot_sync(0xffffffffu, in && pv.le(v)));
+        totR += __popc(__ballot_sync(0xffffffffu, in && pv.ge(v)));
+    }
+    int aL = 0, bB = 0, nswap = 0;
+    for (int q0 = lo; q0 <= hi; q0 += 32) {
+        const int q = q0 + lane;
+        const bool in = q <= hi;
+        const uint32_t v = in ? A.key(q) : 0u;
+        const bool isL = in && pv.le(v), isR = in && pv.ge(v);
+        const unsigned bl = __ballot_sync(0xffffffffu, isL);
+        const unsigned br = __ballot_sync(0xffffffffu, isR);
+        const int a = aL + __popc(bl & lt) + 1;
+        const int b = totR - bB - __popc(br & lt);
+        if (isL) {
+            posL.st(a - 1, q);
+            nswap += (b >= a);
+        }
+        if (isR) posR.st(b - 1, q);
+        aL += __popc(bl);
+        bB += __popc(br);
+    }
+    const int T = (int)__reduce_add_sync(0xffffffffu, (unsigned)nswap);
+    __syncwarp();
+    for (int t = lane; t < T; t += 32) {
+        const int x = posL.ld(t), y = posR.ld(t);
+        if (x != y) {
+            const uint32_t kx = A.key(x), ky = A.key(y);
+            const int ix = A.index(x), iy = A.index(y);
+            A.put(x, ky, iy);
+            A.put(y, kx, ix);
+        }
+    }
+    __syncwarp();
+    final_ij(posL, posR, T, totL, totR, oi, oj);
+    __syncwarp();
+}
+
+constexpr int kTieWarpRange = 512;  // ranges up to this size: one warp per round
+
+// Words of classification bits per warp in a global round: a CTA's slice is
+// at most ceil(V / kTieCluster) elements, a warp's chunk ceil(slice / warps).
+__host__ __device__ __forceinline__ int tie_mask_words(int V) {
+    const int slice = (V + kTieCluster - 1) / kTieCluster;
+    const int chunk = (slice + kTieWarps - 1) / kTieWarps;
+    return (chunk + 31) / 32 + 1;
+}
+
 template <typename T>
 __global__ void __cluster_dims__(kTieCluster, 1, 1) __launch_bounds__(kTieThreads, 3)
 ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __restrict__ ov_n,
@@ -374,6 +493,10 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
     unsigned long long* sk = reinterpret_cast<unsigned long long*>(sposR + kTieSmemRange);  // [kTieSortCap]
     int* ovi = reinterpret_cast<int*>(sk + kTieSortCap);
     float* ovv = reinterpret_cast<float*>(ovi + (ov_stride > 0 ? ov_stride : 1));
+    // classification bits of the global rounds: per warp, words for its chunk
+    const int mwords = tie_mask_words(V);
+    unsigned* maskL = reinterpret_cast<unsigned*>(ovv + (ov_stride > 0 ? ov_stride : 1)) + (threadIdx.x >> 5) * mwords;
+    unsigned* maskR = maskL + kTieWarps * mwords;
 
     cg::cluster_group cluster = cg::this_cluster();
     const int crank = (int)cluster.block_rank();
@@ -444,7 +567,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             const int c0 = min(s0 + warp * wper, s1);
             const int c1 = min(c0 + wper, s1);
             int cl, cr;
-            count_stops(A, c0, c1, pv, &cl, &cr);
+            count_stops_bits(A, c0, c1, pv, maskL, maskR, &cl, &cr);
             int wbL, wbR, ctaL, ctaR;
             tie_warp_scan2(cl, cr, red, &wbL, &wbR, &ctaL, &ctaR);
             if (tid == 0) { xch[0] = ctaL; xch[1] = ctaR; }
@@ -457,7 +580,8 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                 totL += xl;
                 totR += xr;
             }
-            const int nswap = place_stops(A, c0, c1, pv, baseL + wbL, baseR + wbR, totR, gposL, gposR);
+            const int nswap = place_stops_bits(c0, c1, maskL, maskR, baseL + wbL, baseR + wbR, totR, gposL,
+                                               gposR);
             const int ctaS = tie_cta_sum(nswap, red);
             if (tid == 0) xch[2] = ctaS;
             cluster.sync();
@@ -496,7 +620,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                 __syncthreads();
                 const SharedArr S{sK - woff, sI - woff};
                 const SharedPos pL{sposL}, pR{sposR};
-                while (lo < hi && rounds < max_rounds) {
+                while (lo < hi && hi - lo + 1 > kTieWarpRange && rounds < max_rounds) {
                     rounds++;
                     const ProbPivot pv{__uint_as_float(S.key(kk))};
                     int i, j;
@@ -505,6 +629,19 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                     if (i > kk) hi = j;
                     if (lo < woff || hi >= woff + wn || kk < lo || kk > hi) break;
                 }
+                // the last, small rounds by warp 0 alone
+                if (warp == 0) {
+                    while (lo < hi && rounds < max_rounds) {
+                        if (lo < woff || hi >= woff + wn || kk < lo || kk > hi) break;
+                        rounds++;
+                        const ProbPivot pv{__uint_as_float(S.key(kk))};
+                        int i, j;
+                        warp_round(S, pL, pR, lo, hi, pv, &i, &j);
+                        if (j < kk) lo = i;
+                        if (i > kk) hi = j;
+                    }
+                }
+                __syncthreads();
                 // the range's final arrangement (indices; the keys are not read again)
                 for (int q = tid; q < wn; q += kTieThreads) __stcg(A.idx + woff + q, sI[q]);
                 __syncthreads();
@@ -599,7 +736,8 @@ cudaError_t launch_ties_kernel(const T* logits, int V, TieParams prm, const int*
                                int* cand_index, float* cand_prob, int cand_cap, ExpFix fx,
                                cudaStream_t stream, long long* phase_cycles) {
     const size_t smem = 16 * (size_t)kTieSmemRange + 8 * (size_t)kTieSortCap +
-                        8 * (size_t)(ov_stride > 0 ? ov_stride : 1) + 16;
+                        8 * (size_t)(ov_stride > 0 ? ov_stride : 1) +
+                        2 * 4 * (size_t)kTieWarps * tie_mask_words(V) + 16;
     cudaError_t err = cudaFuncSetAttribute(ties_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err != cudaSuccess) return err;
