@@ -107,10 +107,10 @@ __device__ __forceinline__ void load_vec<__nv_bfloat16>(const __nv_bfloat16* p, 
 
 // --------------------------------------------------------------- keys
 // Order-preserving map float -> uint32 (larger float -> larger key).
-__device__ __forceinline__ uint32_t fkey(float f) {
-    uint32_t u = __float_as_uint(f);
+__device__ __forceinline__ uint32_t fkey_bits(uint32_t u) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+__device__ __forceinline__ uint32_t fkey(float f) { return fkey_bits(__float_as_uint(f)); }
 __device__ __forceinline__ float fkey_inv(uint32_t k) {
     uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
     return __uint_as_float(u);

@@ -789,22 +789,29 @@ struct RowOut {
     int row;
 };
 
-// Ranks c candidates by (p desc, index asc) into cd.so, on order-preserving
-// integer keys: the same order as the float probabilities when they are
-// finite, and still a strict total order (so `so` stays a permutation) if a
-// row holds non-finite logits.  Block-wide.
-__device__ __noinline__ void rank_candidates(const Cands& cd, int c) {
+// Ranks c candidates by (p desc, index asc) into cd.so (and, when sp / si
+// are given, the probabilities and indices in that order), on
+// order-preserving integer keys: the same order as the float probabilities
+// when they are finite, and still a strict total order (so `so` stays a
+// permutation) if a row holds non-finite logits.  The keys are formed from
+// the probabilities' stored bits, read as integers: a comparison of two keys
+// formed from float values has been seen to count a NaN as above itself.
+// Block-wide.
+__device__ __noinline__ void rank_candidates(const Cands& cd, int c, float* sp = nullptr, int* si = nullptr) {
     const int tid = threadIdx.x;
+    const uint32_t* pbits = reinterpret_cast<const uint32_t*>(cd.cp);
     if (c <= kRankSortMax) {
         for (int i = tid; i < c; i += kRowThreads) {
-            const uint32_t ki = fkey(cd.cp[i]);
+            const uint32_t bi = pbits[i];
+            const uint32_t ki = fkey_bits(bi);
             const int ii = cd.ci[i];
             int rank = 0;
             for (int j = 0; j < c; j++) {
-                const uint32_t kj = fkey(cd.cp[j]);
+                const uint32_t kj = fkey_bits(pbits[j]);
                 rank += (kj > ki) || (kj == ki && cd.ci[j] < ii);
             }
             cd.so[rank] = i;
+            if (sp) { sp[rank] = __uint_as_float(bi); si[rank] = ii; }
         }
         __syncthreads();
         return;
@@ -812,7 +819,7 @@ __device__ __noinline__ void rank_candidates(const Cands& cd, int c) {
     int npow = 1;
     while (npow < c) npow <<= 1;
     for (int i = tid; i < npow; i += kRowThreads)
-        cd.ck[i] = (i < c) ? (((unsigned long long)fkey(cd.cp[i]) << 32) | (unsigned long long)(uint32_t)i)
+        cd.ck[i] = (i < c) ? (((unsigned long long)fkey_bits(pbits[i]) << 32) | (unsigned long long)(uint32_t)i)
                            : 0ull;
     __syncthreads();
     // ties in p must end in index order: sort keys carry the slot, so
@@ -824,7 +831,7 @@ __device__ __noinline__ void rank_candidates(const Cands& cd, int c) {
         int i = 0;
         while (i < c) {
             int j = i + 1;
-            while (j < c && fkey(cd.cp[cd.so[j]]) == fkey(cd.cp[cd.so[i]])) j++;
+            while (j < c && pbits[cd.so[j]] == pbits[cd.so[i]]) j++;
             for (int a = i + 1; a < j; a++) {  // insertion sort of the run by index
                 const int x = cd.so[a];
                 int b = a - 1;
@@ -835,6 +842,10 @@ __device__ __noinline__ void rank_candidates(const Cands& cd, int c) {
         }
     }
     __syncthreads();
+    if (sp) {
+        for (int i = tid; i < c; i += kRowThreads) { sp[i] = cd.cp[cd.so[i]]; si[i] = cd.ci[cd.so[i]]; }
+        __syncthreads();
+    }
 }
 
 // Candidates by segment maxima, re-read from L2, then min-p / top-p / draw
@@ -1279,11 +1290,34 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
             const float th = seg_thr(g);
             float v[EPL];
             rv.load(g, lane, v);
+            float the[EPL];  // each element's threshold
+#pragma unroll
+            for (int e = 0; e < EPL; e++) { v[e] = __fmul_rn(v[e], inv); the[e] = th; }
+            if (g == 0) {
+                // the row's first segment has no earlier segment: each element
+                // is held against the running maximum of the elements before it
+                float run = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) { the[e] = run; run = fmaxf(run, v[e]); }
+                float x = run;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x = fmaxf(x, y);
+                }
+                float before = __shfl_up_sync(0xffffffffu, x, 1);
+                if (lane == 0) before = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) the[e] = fmaxf(before, the[e]);
+                // the largest running maximum used (that of the segment's last element)
+                lbmax = fmaxf(lbmax, __shfl_sync(0xffffffffu, the[EPL - 1], 31));
+#pragma unroll
+                for (int e = 0; e < EPL; e++) the[e] = __fsub_rn(the[e], kSigGap);
+            }
             unsigned keep = 0;
 #pragma unroll
             for (int e = 0; e < EPL; e++) {
-                v[e] = __fmul_rn(v[e], inv);
-                const bool k = (g * SEG + lane * EPL + e < V) && v[e] >= th;
+                const bool k = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
                 keep |= (k ? 1u : 0u) << e;
             }
             const int cnt = __popc(keep);
@@ -1441,11 +1475,14 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
         __syncthreads();
         const int c = sh.ncand;
         if (c >= 1 && c <= kRankSortMax && c <= ccap) {
-            rank_candidates(cd, c);
+            // the candidates in rank order: probabilities in ct, indices in ck
+            float* sp = cd.ct;
+            int* si = reinterpret_cast<int*>(cd.ck);
+            rank_candidates(cd, c, sp, si);
             stamp(7);
             if (tid == 0) {
-                auto P = [&](int i) { return cd.cp[cd.so[i]]; };
-                auto I = [&](int i) { return cd.ci[cd.so[i]]; };
+                auto P = [&](int i) { return sp[i]; };
+                auto I = [&](int i) { return si[i]; };
                 // probabilities an element outside the stash can reach: at most p(theta)
                 const float ptheta = complete ? 0.0f : __fmul_rn(exact_exp(__fsub_rn(theta, M), fx), sum_inv);
                 int cert = c;  // leading positions whose element and probability are certain

@@ -52,6 +52,34 @@ def test_topk_above_segment_count(oracle):
     compare(wl, g, o)
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("pi", [0, 1])
+def test_first_segment_running_maximum(oracle, dtype, pi):
+    """Rows whose first 256 elements rise, fall, stay flat or hold one spike:
+    the first segment has no earlier segment to bound its stash threshold,
+    so each of its elements is held against the running maximum before it."""
+    V, B = 4096, 8
+    g = np.random.default_rng(7 + pi)
+    x = g.normal(0, 2.0, size=(B, V)).astype(np.float32)
+    ramp = np.linspace(-10, 10, 256, dtype=np.float32)
+    x[0, :256] = ramp             # every element a new running maximum
+    x[1, :256] = ramp[::-1]       # the first element the maximum of the segment
+    x[2, :256] = -30.0
+    x[2, 0] = 5.0
+    x[3, :256] = -30.0
+    x[3, 255] = 12.0
+    x[4, :256] = 0.3 * ramp       # a ramp inside the significance gap
+    x[5, :256] = 0.0              # ties all along
+    x[6, 0] = 40.0                # an early spike that dominates the row
+    x[7, 100:110] = 15.0
+    logits = W.to_bf16_bits(x) if dtype == "bf16" else x
+    ids = g.integers(0, V, size=B * 16)
+    wl = W._full_window(B, 16, ids, 300 + pi, f"first_segment_{dtype}_{pi}", PARAMS[pi], logits, dtype)
+    o = oracle.sample_workload(wl, debug=True, cand_cap=64)
+    gg = run_gpu(wl)
+    compare(wl, gg, o)
+
+
 def test_large_topk_full_vocab(oracle):
     wl = W.topk_bf16(B=8, seed=12)
     wl.params = W.SamplingParams(1.0, 0.999, 0.0, 1000, 1.15, 0.0, 0.0)
