@@ -17,7 +17,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libqwen600_sampler.so")
-SOURCES = ["qs_row.cu", "qs_ties.cu", "qs_api.cu", "qs_static.cu", "qs_lmhead.cu"]
+SOURCES = ["qs_row.cu", "qs_ties.cu", "qs_sort.cu", "qs_api.cu", "qs_static.cu", "qs_lmhead.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "--fmad=false", "-std=c++17", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-I", CSRC,

@@ -33,6 +33,10 @@ cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*,
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, float*, cudaStream_t);
 template <typename T>
+cudaError_t launch_sort_kernel(const T*, int, float, float, int, const int*, const int*, const float*,
+                               int, const int*, const int*, RowResult*, uint32_t*, uint32_t*, int, int*,
+                               float*, int, ExpFix, cudaStream_t);
+template <typename T>
 cudaError_t launch_probs(const T*, int, int, const int*, const int*, const float*, int,
                          const RowResult*, float*, ExpFix, cudaStream_t);
 
@@ -456,6 +460,26 @@ static int run(qs_sampler* s, const Call& c) {
                 (const __nv_bfloat16*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val, s->ov_stride,
                 s->slow_list, s->slow_count, s->res, s->tie_scratch, s->tie_pos, nct, c.cand_index,
                 c.cand_prob, c.cand_cap, s->fix(), c.stream));
+        }
+    }
+    if (!greedy && !(topk && !(c.flags & QS_FLAG_INDEX_TIES))) {
+        // rows queued by the row kernel: the full sort (its scratch is the tie
+        // pass's, which does not run in this mode)
+        KernelScope ks(s, 2, c.stream);
+        const int nct = B < s->tie_ctas ? B : s->tie_ctas;
+        uint32_t* bufA = reinterpret_cast<uint32_t*>(s->tie_scratch);
+        uint32_t* bufB = reinterpret_cast<uint32_t*>(s->tie_pos);
+        const int k = topk ? p.top_k : 0;
+        if (c.dtype == QS_F32) {
+            CK(launch_sort_kernel<float>((const float*)c.logits, V, p.topp, p.minp, k, ovn, s->ov_idx,
+                                         s->ov_val, s->ov_stride, s->slow_list, s->slow_count, s->res,
+                                         bufA, bufB, nct, c.cand_index, c.cand_prob, c.cand_cap,
+                                         s->fix(), c.stream));
+        } else {
+            CK(launch_sort_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, V, p.topp, p.minp, k,
+                                                 ovn, s->ov_idx, s->ov_val, s->ov_stride, s->slow_list,
+                                                 s->slow_count, s->res, bufA, bufB, nct, c.cand_index,
+                                                 c.cand_prob, c.cand_cap, s->fix(), c.stream));
         }
     }
     if (c.probs) {

@@ -957,16 +957,16 @@ __device__ __noinline__ void finish_by_segments(RowView<T> rv, int nseg, const f
     if (ph && tid == 0) ph[7] = clock64();
 
     if (status != 0) {
-        // the fast kernel cannot hold this row's candidates; the exact pass
-        // redoes the whole selection from the materialised row (top-k mode)
+        // the fast kernel cannot hold this row's candidates; an exact pass
+        // redoes the whole selection from the row: the tie replay (top-k,
+        // qs_ties.cu) or the full sort (no top-k, or ties in index order,
+        // qs_sort.cu)
         if (tid == 0) {
             out.status = status;
             out.token = -1;
-            if (use_topk && !(prm.flags & QS_FLAG_INDEX_TIES)) {
-                const int slot = atomicAdd(ro.slow_count, 1);
-                ro.slow_list[slot] = ro.row;
-                out.exact_ties = 1;
-            }
+            const int slot = atomicAdd(ro.slow_count, 1);
+            ro.slow_list[slot] = ro.row;
+            out.exact_ties = (use_topk && !(prm.flags & QS_FLAG_INDEX_TIES)) ? 1 : 0;
             ro.res[ro.row] = out;
         }
         return;
