@@ -21,8 +21,8 @@ namespace qs {
 
 template <typename T>
 cudaError_t launch_row_kernel(const T*, int, int, RowParams, RowWindow, unsigned long long*,
-                              RowResult*, int*, int*, int*, float*, int, ExpFix, cudaStream_t,
-                              long long* phase_cycles = nullptr);
+                              RowResult*, int*, int*, int*, float*, int, ExpFix, RowScratch,
+                              cudaStream_t, long long* phase_cycles = nullptr);
 cudaError_t launch_write_penalized(float*, int, int, const int*, const int*, const float*, int,
                                    cudaStream_t);
 template <typename T>
@@ -111,6 +111,14 @@ struct qs_sampler {
     __nv_bfloat16* lh_logits = nullptr;  // [max_batch, vocab]
     int* lh_err = nullptr;
     ExpFix fix() const { return ExpFix{exp_off, exp_ent, exp_bloom, (uint32_t)QS_EXP_NB}; }
+    // the row kernel's hand-over from its streaming to its finishing pass
+    float* rs_segm = nullptr;
+    float* rs_st_t = nullptr;
+    int* rs_st_i = nullptr;
+    int* rs_meta = nullptr;
+    RowScratch scratch() const {
+        return RowScratch{rs_segm, rs_st_t, rs_st_i, rs_meta, row_scratch_seg_stride(vocab)};
+    }
     // launch accounting and optional per-kernel event timing
     bool profiling = false;
     qs_profile prof{};
@@ -174,7 +182,8 @@ static void release(qs_sampler* s) {
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts, s->slot_counts,
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
-                    s->lh_normed, s->lh_logits, s->lh_err};
+                    s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm, s->rs_st_t, s->rs_st_i,
+                    s->rs_meta};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
@@ -266,6 +275,10 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     ALLOC(s->tie_scratch, sizeof(unsigned long long) * V * s->tie_ctas);
     ALLOC(s->tie_pos, sizeof(int) * 2 * V * s->tie_ctas);
     ALLOC(s->rng, sizeof(unsigned long long) * B);
+    ALLOC(s->rs_segm, sizeof(float) * B * (size_t)row_scratch_seg_stride(vocab));
+    ALLOC(s->rs_st_t, sizeof(float) * B * (size_t)kStashCap);
+    ALLOC(s->rs_st_i, sizeof(int) * B * (size_t)kStashCap);
+    ALLOC(s->rs_meta, sizeof(int) * 4 * B);
     ALLOC(s->d_in, sizeof(float) * B * V);
     ALLOC(s->d_tok, sizeof(int) * B);
     ALLOC(s->exp_off, sizeof(qs_exp_fix_off));
@@ -439,11 +452,11 @@ static int run(qs_sampler* s, const Call& c) {
     if (c.dtype == QS_F32) {
         CK(launch_row_kernel<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res,
                                     s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
-                                    c.cand_cap, s->fix(), c.stream));
+                                    c.cand_cap, s->fix(), s->scratch(), c.stream));
     } else {
         CK(launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng,
                                             s->res, s->slow_list, s->slow_count, c.cand_index,
-                                            c.cand_prob, c.cand_cap, s->fix(), c.stream));
+                                            c.cand_prob, c.cand_cap, s->fix(), s->scratch(), c.stream));
     }
     }
     if (!greedy && topk && !(c.flags & QS_FLAG_INDEX_TIES)) {

@@ -33,6 +33,22 @@ struct RowParams {
     int top_k;
     unsigned flags;
 };
+constexpr int kStashCap = 1536;  // stashed elements per row before the dense method
+
+// What the row kernel's streaming pass leaves for its finishing pass, per row
+// (global memory): the penalised segment maxima, the stash (t and index; each
+// stashed segment's elements contiguous) and [nst, overflow, max lb key, 0].
+struct RowScratch {
+    float* segm;   // [rows][seg_stride]
+    float* st_t;   // [rows][kStashCap]
+    int* st_i;     // [rows][kStashCap]
+    int* meta;     // [rows][4]
+    int seg_stride;
+};
+// Segment maxima per row that fit either element type (fp32 segments are the
+// shorter: 128 elements).
+inline int row_scratch_seg_stride(int V) { return (V + 127) / 128; }
+
 struct TieParams {
     float temperature, topp, minp;
     int top_k;

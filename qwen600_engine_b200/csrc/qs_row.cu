@@ -57,9 +57,12 @@ constexpr int kRowWarps = kRowThreads / 32;
 #ifndef QS_ROW_ROUND
 #define QS_ROW_ROUND 64
 #endif
-constexpr int kRowMinBlocks = QS_ROW_MIN_BLOCKS;  // resident rows per SM the registers are sized for
+constexpr int kRowMinBlocks = QS_ROW_MIN_BLOCKS;  // finishing pass: resident rows per SM the registers are sized for
+#ifndef QS_STREAM_MIN_BLOCKS
+#define QS_STREAM_MIN_BLOCKS 3
+#endif
+constexpr int kStreamMinBlocks = QS_STREAM_MIN_BLOCKS;  // streaming pass: resident rows per SM
 constexpr int kRowRound = QS_ROW_ROUND;  // segments per streaming round (kRowRound / 8 per warp)
-constexpr int kStashCap = 1536;          // stashed elements per row before the dense method
 static_assert((kRowRound == 32 || kRowRound == 64) && kRowRound % kRowWarps == 0, "round layout");
 constexpr int kRankSortMax = 512;  // candidates ranked by counting up to this many
 constexpr float kDelta = 1e-5f;    // binade prediction margin (misses only cost a replay)
@@ -1042,13 +1045,14 @@ __device__ __noinline__ void finish_by_segments(RowView<T> rv, int nseg, const f
     }
 }
 
+// Streaming pass: the window's penalties, the row's segment maxima and the
+// stash, left in `scr` for row_finish_kernel; greedy rows are finished here.
+// Its shared memory ends where the finishing pass's stash region begins.
 template <typename T>
-__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
-row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
-           unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
-           int* __restrict__ slow_list, int* __restrict__ slow_count,
-           int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
-           ExpFix fx, int ccap, int scap, long long* __restrict__ phase_cycles) {
+__global__ void __launch_bounds__(kRowThreads, kStreamMinBlocks)
+row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
+                  RowResult* __restrict__ res, RowScratch scr, int ccap, int scap,
+                  long long* __restrict__ phase_cycles) {
     constexpr int EPL = Elem<T>::kPerLane;
     constexpr int SEG = 32 * EPL;
     constexpr int U = kRowRound / kRowWarps;  // segments in flight per warp in the streaming pass
@@ -1068,31 +1072,46 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
     unsigned long long* pairs = (unsigned long long*)(smem + L.pairs);
     float* pcnt = (float*)(smem + L.pcnt);
     uint32_t* pubr = (uint32_t*)(smem + L.pubr);      // per streaming round: max key seen
-    unsigned char* region = smem + L.region;          // stash, or the dense method's tables
-    float* st_t = (float*)region;
-    int* st_i = (int*)(region + 4 * (size_t)scap);
-    float* st_e = (float*)(region + 8 * (size_t)scap);   // expf(t - max), the reference's term
-    float* slist = (float*)(region + 12 * (size_t)scap); // terms in index order
-    int* sstart = (int*)(region + 16 * (size_t)scap);
-    int* scnt = sstart + nseg;
-    const Cands cd{(float*)(smem + L.ct), (int*)(smem + L.ci), (float*)(smem + L.cp),
-                   (int*)(smem + L.so), (unsigned long long*)(smem + L.ck),
-                   (uint32_t*)(smem + L.rhist), ccap};
+    // the stash goes straight to the row's scratch
+    float* st_t = scr.st_t ? scr.st_t + (size_t)row * scap : nullptr;
+    int* st_i = scr.st_i ? scr.st_i + (size_t)row * scap : nullptr;
     __shared__ RowShared sh;
-    const RowOut ro{res, slow_list, slow_count, cand_index_out, cand_prob_out, cand_cap, row};
 
-    long long* ph = phase_cycles ? phase_cycles + (size_t)row * 10 : nullptr;
+    long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
     auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
     stamp(0);
 
     const bool greedy = prm.temperature < 1e-6f;
     const float inv = greedy ? 1.0f : __fdiv_rn(1.0f, prm.temperature);
 
+    RowView<T> rv;
+    rv.L = logits + (size_t)row * V;
+    rv.V = V;
+    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
+    rv.segov = segov;
+    rv.ovi = ovi;
+    rv.ovv = ovv;
+    rv.nov = 0;
+    // the streaming pass keeps one round of vectors in flight per warp; the
+    // first round is requested before the window is read, so its loads
+    // overlap the construction of the penalty tables
+    uint4 r[U];
+    auto request = [&](int jj) {
+        const int gb = jj * kRowRound + warp;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int g = gb + u * kRowWarps;
+            if ((g < nseg) && rv.full(g, lane)) r[u] = rv.raw(g, lane);
+            else r[u] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    request(0);
+
     // ---- the row's penalty window (sampler.h:114-141): slots sorted by
     // (token, slot), distinct tokens and the slot range of each; the values
     // are formed from the raw logits as the streaming pass reads them
     if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); sh.misc[7] = 0; }
-    for (int g = tid; g < nseg; g += kRowThreads) { segov[g] = 0; scnt[g] = 0; }
+    for (int g = tid; g < nseg; g += kRowThreads) segov[g] = 0;
     for (int j = tid; j < L.nrounds; j += kRowThreads) pubr[j] = fkey(-INFINITY);
     int cntw = (win.hist && win.count) ? win.count[row] : 0;
     cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
@@ -1179,13 +1198,6 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
     if (tid == 0 && win.ov_n) win.ov_n[row] = nov;
     __syncthreads();
 
-    RowView<T> rv;
-    rv.L = logits + (size_t)row * V;
-    rv.V = V;
-    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
-    rv.segov = segov;
-    rv.ovi = ovi;
-    rv.ovv = ovv;
     rv.nov = nov;
     stamp(1);
 
@@ -1196,18 +1208,8 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
     // published for earlier rounds).
     float lb = -INFINITY;
     float lbmax = -INFINITY;  // largest lb used: the stash holds every t >= lbmax - 17.5
-    uint4 r[U];  // this round's vectors; the next round's are requested as soon as
-                 // this round's maxima are taken (the stash re-reads from L2)
-    auto request = [&](int jj) {
-        const int gb = jj * kRowRound + warp;
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int g = gb + u * kRowWarps;
-            if ((g < nseg) && rv.full(g, lane)) r[u] = rv.raw(g, lane);
-            else r[u] = make_uint4(0u, 0u, 0u, 0u);
-        }
-    };
-    request(0);
+    // r holds this round's vectors; the next round's are requested as soon as
+    // this round's maxima are taken (the stash re-reads from L2)
     for (int j = 0; j < L.nrounds; j++) {
         const int g0 = j * kRowRound + warp;
         unsigned slow = 0;  // segments that are partial or hold overrides (warp-uniform)
@@ -1223,19 +1225,25 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
                 }
             }
         }
-        if (j + 1 < L.nrounds) request(j + 1);
         while (slow) {
             const int u = __ffs(slow) - 1;
             slow &= slow - 1;
             const int g = g0 + u * kRowWarps;
+            // the segment's vector is still in r[u] (partial lanes and window
+            // tokens are resolved by widen)
+            uint4 ru = r[0];
+#pragma unroll
+            for (int q = 1; q < U; q++)
+                if (q == u) ru = r[q];
             float v[EPL];
-            rv.load(g, lane, v);
+            rv.widen(g, lane, rv.full(g, lane), ru, v);
             float m = v[0];
 #pragma unroll
             for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
             const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
             if (lane == 0) segm[g] = fkey_inv(km);
         }
+        if (j + 1 < L.nrounds) request(j + 1);  // r is free: every maximum of this round is taken
         __syncwarp();
         if (greedy) continue;
         // stash thresholds: round 0 per segment from exact prefix maxima
@@ -1332,7 +1340,6 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
             if (lane == 0) base = atomicAdd(&sh.nst, tot);
             base = __shfl_sync(0xffffffffu, base, 0);
             if (base + tot <= scap) {
-                if (lane == 0) { sstart[g] = base; scnt[g] = tot; }
                 int pos = base + incl - cnt;
 #pragma unroll
                 for (int e = 0; e < EPL; e++) {
@@ -1385,6 +1392,107 @@ row_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
         }
         return;
     }
+
+    // ---- hand over to the finishing pass
+    for (int g = tid; g < nseg; g += kRowThreads) scr.segm[(size_t)row * scr.seg_stride + g] = segm[g];
+    if (tid == 0) {
+        int* m = scr.meta + (size_t)row * 4;
+        m[0] = sh.nst;
+        m[1] = sh.ovf;
+        m[2] = (int)sh.maxlb;
+        m[3] = 0;
+    }
+}
+
+// Finishing pass (non-greedy rows): the exact softmax denominator, the
+// candidates, min-p / top-p and the draw, from what row_stream_kernel left in
+// `scr`; rows it cannot settle go to the exact passes.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
+row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
+                  unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
+                  int* __restrict__ slow_list, int* __restrict__ slow_count,
+                  int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
+                  ExpFix fx, int ccap, int scap, RowScratch scr, long long* __restrict__ phase_cycles) {
+    constexpr int EPL = Elem<T>::kPerLane;
+    constexpr int SEG = 32 * EPL;
+    const int row = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const RowSmem L(V, SEG, win.window, ccap, scap);
+    const int nseg = L.nseg;
+
+    // ---- shared memory carve-up
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* segm = (float*)(smem + L.segm);            // segment maxima (l, then t)
+    uint32_t* segk = (uint32_t*)(smem + L.segk);      // order keys of segm (t)
+    unsigned char* segov = smem + L.segov;
+    int* ovi = (int*)(smem + L.ovi);
+    float* ovv = (float*)(smem + L.ovv);
+    unsigned char* region = smem + L.region;          // stash, or the dense method's tables
+    float* st_t = (float*)region;
+    int* st_i = (int*)(region + 4 * (size_t)scap);
+    float* st_e = (float*)(region + 8 * (size_t)scap);   // expf(t - max), the reference's term
+    float* slist = (float*)(region + 12 * (size_t)scap); // terms in index order
+    int* sstart = (int*)(region + 16 * (size_t)scap);
+    int* scnt = sstart + nseg;
+    const Cands cd{(float*)(smem + L.ct), (int*)(smem + L.ci), (float*)(smem + L.cp),
+                   (int*)(smem + L.so), (unsigned long long*)(smem + L.ck),
+                   (uint32_t*)(smem + L.rhist), ccap};
+    __shared__ RowShared sh;
+    const RowOut ro{res, slow_list, slow_count, cand_index_out, cand_prob_out, cand_cap, row};
+
+    long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
+    auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
+    stamp(10);
+    const float inv = __fdiv_rn(1.0f, prm.temperature);
+
+    // ---- what the streaming pass left: segment maxima, the window's
+    // overrides, the stash (each segment's start and count rebuilt here)
+    const int* meta = scr.meta + (size_t)row * 4;
+    const int nst_in = meta[0], ovf_in = meta[1];
+    const uint32_t maxlb_in = (uint32_t)meta[2];
+    const int nov = (win.ov_n && win.ov_idx) ? win.ov_n[row] : 0;
+    for (int g = tid; g < nseg; g += kRowThreads) {
+        segm[g] = scr.segm[(size_t)row * scr.seg_stride + g];
+        segov[g] = 0;
+        scnt[g] = 0;
+        sstart[g] = 0x7fffffff;
+    }
+    if (tid == 0) { sh.nst = nst_in; sh.ovf = ovf_in; sh.maxlb = maxlb_in; }
+    __syncthreads();
+    for (int j = tid; j < nov; j += kRowThreads) {
+        const int q = win.ov_idx[(size_t)row * win.ov_stride + j];
+        ovi[j] = q;
+        ovv[j] = win.ov_val[(size_t)row * win.ov_stride + j];
+        segov[q / SEG] = 1;
+    }
+    if (!ovf_in) {
+        for (int i = tid; i < nst_in; i += kRowThreads) {
+            const int q = scr.st_i[(size_t)row * scap + i];
+            st_t[i] = scr.st_t[(size_t)row * scap + i];
+            st_i[i] = q;
+            atomicAdd(&scnt[q / SEG], 1);
+            atomicMin(&sstart[q / SEG], i);
+        }
+    }
+    __syncthreads();
+    RowView<T> rv;
+    rv.L = logits + (size_t)row * V;
+    rv.V = V;
+    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
+    rv.segov = segov;
+    rv.ovi = ovi;
+    rv.ovv = ovv;
+    rv.nov = nov;
+    float lm = -INFINITY;
+    for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
+    const float maxl = rblock_max(lm, sh.red_f);
+
+    RowResult out;
+    out.token = 0; out.greedy = 0; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
+    out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0; out.max_logit = maxl;
+    out.sum = 0.f; out.r = 0.f; out.renorm_sum = 0.f; out.inv_temp = 0.f; out.sum_inv = 0.f;
+    out.status = 0; out.pad_ = 0;
 
     // ---- B: temperature on the segment maxima; the row's uniform
     const float M = __fmul_rn(maxl, inv);
@@ -1583,34 +1691,43 @@ int row_kernel_ccap(int top_k, int V) {
     return c;
 }
 
-size_t row_kernel_smem(int V, int dtype_bytes, int window, int ccap) {
-    const RowSmem L(V, 32 * (16 / dtype_bytes), window, ccap, kStashCap);
-    return L.total;
-}
-
+// The streaming pass, then (non-greedy calls) the finishing pass.  `scr`
+// must hold `B` rows of row_scratch_seg_stride(V) segment maxima and
+// kStashCap stash entries unless the call is greedy.
 template <typename T>
 cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, RowWindow win,
                               unsigned long long* rng, RowResult* res, int* slow_list,
                               int* slow_count, int* cand_index, float* cand_prob, int cand_cap,
-                              ExpFix fx, cudaStream_t stream, long long* phase_cycles) {
+                              ExpFix fx, RowScratch scr, cudaStream_t stream, long long* phase_cycles) {
     const int ccap = row_kernel_ccap(prm.top_k, V);
     if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
-    const size_t smem = row_kernel_smem(V, (int)sizeof(T), win.window, ccap);
-    cudaError_t err = cudaFuncSetAttribute(row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)smem);
+    const bool greedy = prm.temperature < 1e-6f;
+    if (!greedy && (!scr.segm || !scr.st_t || !scr.st_i || !scr.meta ||
+                    scr.seg_stride < row_scratch_seg_stride(V)))
+        return cudaErrorInvalidValue;
+    const RowSmem L(V, 32 * (16 / (int)sizeof(T)), win.window, ccap, kStashCap);
+    cudaError_t err = cudaFuncSetAttribute(row_stream_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)L.region);
     if (err != cudaSuccess) return err;
-    row_kernel<T><<<B, kRowThreads, smem, stream>>>(logits, V, prm, win, rng, res, slow_list,
-                                                    slow_count, cand_index, cand_prob, cand_cap, fx,
-                                                    ccap, kStashCap, phase_cycles);
+    row_stream_kernel<T><<<B, kRowThreads, L.region, stream>>>(logits, V, prm, win, res, scr, ccap,
+                                                               kStashCap, phase_cycles);
+    err = cudaGetLastError();
+    if (err != cudaSuccess || greedy) return err;
+    err = cudaFuncSetAttribute(row_finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)L.total);
+    if (err != cudaSuccess) return err;
+    row_finish_kernel<T><<<B, kRowThreads, L.total, stream>>>(logits, V, prm, win, rng, res, slow_list,
+                                                              slow_count, cand_index, cand_prob, cand_cap,
+                                                              fx, ccap, kStashCap, scr, phase_cycles);
     return cudaGetLastError();
 }
 
 template cudaError_t launch_row_kernel<float>(const float*, int, int, RowParams, RowWindow,
                                               unsigned long long*, RowResult*, int*, int*, int*,
-                                              float*, int, ExpFix, cudaStream_t, long long*);
+                                              float*, int, ExpFix, RowScratch, cudaStream_t, long long*);
 template cudaError_t launch_row_kernel<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams,
                                                       RowWindow, unsigned long long*, RowResult*,
-                                                      int*, int*, int*, float*, int, ExpFix,
+                                                      int*, int*, int*, float*, int, ExpFix, RowScratch,
                                                       cudaStream_t, long long*);
 
 // QS_FLAG_WRITE_PENALIZED: the reference's in-place penalty update of fp32

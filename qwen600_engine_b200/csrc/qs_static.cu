@@ -31,8 +31,8 @@ namespace qs {
 
 template <typename T>
 cudaError_t launch_row_kernel(const T*, int, int, RowParams, RowWindow, unsigned long long*,
-                              RowResult*, int*, int*, int*, float*, int, ExpFix, cudaStream_t,
-                              long long* phase_cycles);
+                              RowResult*, int*, int*, int*, float*, int, ExpFix, RowScratch,
+                              cudaStream_t, long long* phase_cycles);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, float*, cudaStream_t);
 
@@ -123,12 +123,12 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
     const ExpFix none{nullptr, nullptr, nullptr, 0u};
     if (dtype == QS_F32)
         e = launch_row_kernel<float>((const float*)d_logits, batch, vocab, rp, win, sc->rng, sc->res,
-                                     sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none, st,
-                                     nullptr);
+                                     sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none,
+                                     RowScratch{}, st, nullptr);
     else
         e = launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, rp, win,
                                              sc->rng, sc->res, sc->slow_list, sc->slow_count,
-                                             nullptr, nullptr, 0, none, st, nullptr);
+                                             nullptr, nullptr, 0, none, RowScratch{}, st, nullptr);
     if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "row kernel", cudaGetErrorString(e));
     e = launch_emit(batch, vocab, 0, sc->res, d_tokens, nullptr, nullptr, nullptr, nullptr, nullptr,
                     nullptr, st);
