@@ -113,12 +113,7 @@ struct qs_sampler {
     ExpFix fix() const { return ExpFix{exp_off, exp_ent, exp_bloom, (uint32_t)QS_EXP_NB}; }
     // the row kernel's hand-over from its streaming to its finishing pass
     float* rs_segm = nullptr;
-    float* rs_st_t = nullptr;
-    int* rs_st_i = nullptr;
-    int* rs_meta = nullptr;
-    RowScratch scratch() const {
-        return RowScratch{rs_segm, rs_st_t, rs_st_i, rs_meta, row_scratch_seg_stride(vocab)};
-    }
+    RowScratch scratch() const { return RowScratch{rs_segm, row_scratch_seg_stride(vocab)}; }
     // launch accounting and optional per-kernel event timing
     bool profiling = false;
     qs_profile prof{};
@@ -182,8 +177,7 @@ static void release(qs_sampler* s) {
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts, s->slot_counts,
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
-                    s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm, s->rs_st_t, s->rs_st_i,
-                    s->rs_meta};
+                    s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
@@ -276,9 +270,6 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     ALLOC(s->tie_pos, sizeof(int) * 2 * V * s->tie_ctas);
     ALLOC(s->rng, sizeof(unsigned long long) * B);
     ALLOC(s->rs_segm, sizeof(float) * B * (size_t)row_scratch_seg_stride(vocab));
-    ALLOC(s->rs_st_t, sizeof(float) * B * (size_t)kStashCap);
-    ALLOC(s->rs_st_i, sizeof(int) * B * (size_t)kStashCap);
-    ALLOC(s->rs_meta, sizeof(int) * 4 * B);
     ALLOC(s->d_in, sizeof(float) * B * V);
     ALLOC(s->d_tok, sizeof(int) * B);
     ALLOC(s->exp_off, sizeof(qs_exp_fix_off));

@@ -36,13 +36,9 @@ struct RowParams {
 constexpr int kStashCap = 1536;  // stashed elements per row before the dense method
 
 // What the row kernel's streaming pass leaves for its finishing pass, per row
-// (global memory): the penalised segment maxima, the stash (t and index; each
-// stashed segment's elements contiguous) and [nst, overflow, max lb key, 0].
+// (global memory): the penalised segment maxima.
 struct RowScratch {
     float* segm;   // [rows][seg_stride]
-    float* st_t;   // [rows][kStashCap]
-    int* st_i;     // [rows][kStashCap]
-    int* meta;     // [rows][4]
     int seg_stride;
 };
 // Segment maxima per row that fit either element type (fp32 segments are the

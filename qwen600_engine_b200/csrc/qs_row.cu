@@ -59,7 +59,7 @@ constexpr int kRowWarps = kRowThreads / 32;
 #endif
 constexpr int kRowMinBlocks = QS_ROW_MIN_BLOCKS;  // finishing pass: resident rows per SM the registers are sized for
 #ifndef QS_STREAM_MIN_BLOCKS
-#define QS_STREAM_MIN_BLOCKS 3
+#define QS_STREAM_MIN_BLOCKS 4
 #endif
 constexpr int kStreamMinBlocks = QS_STREAM_MIN_BLOCKS;  // streaming pass: resident rows per SM
 constexpr int kRowRound = QS_ROW_ROUND;  // segments per streaming round (kRowRound / 8 per warp)
@@ -477,8 +477,8 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
 
 // Shared-memory layout of one row, shared by the kernel and its launcher.
 struct RowSmem {
-    size_t segm, segk, segov, ovi, ovv, ofirst, pairs, pcnt, pubr, region, ct, ci, cp, so, ck, rhist,
-        total;
+    size_t segm, segk, segov, ovi, ovv, ofirst, pairs, pcnt, pubr, hotl, region, ct, ci, cp, so, ck,
+        rhist, total;
     int nseg, nrounds, scap, ccap, npairs;
     __host__ __device__ static size_t r16(size_t b) { return (b + 15) & ~(size_t)15; }
     __host__ __device__ RowSmem(int V, int seg, int ov_stride, int ccap_, int scap_) {
@@ -499,6 +499,7 @@ struct RowSmem {
         pairs = p; p += r16(16 * (size_t)npairs);  // sorted pairs + a second buffer
         pcnt = p; p += r16(4 * ovs);
         pubr = p; p += r16(4 * (size_t)nrounds);
+        hotl = p; p += r16(4 * (size_t)nseg);
         region = p;
         const size_t fast = 16 * (size_t)scap + 8 * (size_t)nseg;  // stash t, i, e, ordered terms; tables
         const size_t slow = 32 * (size_t)nseg;                      // hot, hthr, hA, hE, Tf
@@ -1072,9 +1073,6 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     unsigned long long* pairs = (unsigned long long*)(smem + L.pairs);
     float* pcnt = (float*)(smem + L.pcnt);
     uint32_t* pubr = (uint32_t*)(smem + L.pubr);      // per streaming round: max key seen
-    // the stash goes straight to the row's scratch
-    float* st_t = scr.st_t ? scr.st_t + (size_t)row * scap : nullptr;
-    int* st_i = scr.st_i ? scr.st_i + (size_t)row * scap : nullptr;
     __shared__ RowShared sh;
 
     long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
@@ -1201,15 +1199,9 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     rv.nov = nov;
     stamp(1);
 
-    // ---- A: streaming pass.  Segment maxima of the penalised logits, and a
-    // stash of every element that may be significant for the softmax sum:
-    // t >= lb - 17.5 where lb is a lower bound of the maximum t over the
-    // segments before it (exact for the first round; afterwards the maxima
-    // published for earlier rounds).
-    float lb = -INFINITY;
-    float lbmax = -INFINITY;  // largest lb used: the stash holds every t >= lbmax - 17.5
-    // r holds this round's vectors; the next round's are requested as soon as
-    // this round's maxima are taken (the stash re-reads from L2)
+    // ---- A: streaming pass: the maximum of each segment of the penalised
+    // logits.  r holds this round's vectors; the next round's are requested
+    // as soon as this round's maxima are taken.
     for (int j = 0; j < L.nrounds; j++) {
         const int g0 = j * kRowRound + warp;
         unsigned slow = 0;  // segments that are partial or hold overrides (warp-uniform)
@@ -1244,118 +1236,7 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
             if (lane == 0) segm[g] = fkey_inv(km);
         }
         if (j + 1 < L.nrounds) request(j + 1);  // r is free: every maximum of this round is taken
-        __syncwarp();
-        if (greedy) continue;
-        // stash thresholds: round 0 per segment from exact prefix maxima
-        // (lane i holds those of its kRowRound / 32 segments), later rounds one
-        float pa = -INFINITY, pb = -INFINITY, thr_all = -INFINITY;
-        if (j == 0) {
-            __syncthreads();
-            constexpr int SPL = kRowRound / 32;  // segments per lane (1 or 2)
-            const int a = SPL * lane, b = SPL * lane + 1;
-            const float ta = a < nseg ? __fmul_rn(segm[a], inv) : -INFINITY;
-            const float tb = (SPL == 2 && b < nseg) ? __fmul_rn(segm[b], inv) : -INFINITY;
-            float x = fmaxf(ta, tb);
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float y = __shfl_up_sync(0xffffffffu, x, o);
-                if (lane >= o) x = fmaxf(x, y);
-            }
-            pa = __shfl_up_sync(0xffffffffu, x, 1);
-            if (lane == 0) pa = -INFINITY;
-            pb = fmaxf(pa, ta);
-            lb = __shfl_sync(0xffffffffu, x, 31);  // maximum of the whole first round
-        } else {
-            lb = fmaxf(lb, fkey_inv(*(volatile uint32_t*)&pubr[j - 1]));
-            lbmax = fmaxf(lbmax, lb);
-            thr_all = __fsub_rn(lb, kSigGap);
-        }
-        auto seg_thr = [&](int g) {  // warp-uniform g
-            if (j != 0) return thr_all;
-            constexpr int SPL = kRowRound / 32;
-            const int src = (g % kRowRound) / SPL;
-            const float qa = __shfl_sync(0xffffffffu, pa, src);
-            const float qb = __shfl_sync(0xffffffffu, pb, src);
-            return __fsub_rn((SPL == 2 && (g & 1)) ? qb : qa, kSigGap);
-        };
-        float rmax = -INFINITY;
-        unsigned want = 0;
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int g = g0 + u * kRowWarps;
-            const float th = seg_thr(g);
-            if (g >= nseg) continue;
-            if (j == 0) lbmax = fmaxf(lbmax, __fadd_rn(th, kSigGap));
-            const float tmax = __fmul_rn(segm[g], inv);
-            rmax = fmaxf(rmax, tmax);
-            if (tmax >= th) want |= 1u << u;
-        }
-        if (*(volatile int*)&sh.ovf) want = 0;  // the dense method takes over; stop stashing
-        while (want) {
-            const int u = __ffs(want) - 1;
-            want &= want - 1;
-            const int g = g0 + u * kRowWarps;
-            const float th = seg_thr(g);
-            float v[EPL];
-            rv.load(g, lane, v);
-            float the[EPL];  // each element's threshold
-#pragma unroll
-            for (int e = 0; e < EPL; e++) { v[e] = __fmul_rn(v[e], inv); the[e] = th; }
-            if (g == 0) {
-                // the row's first segment has no earlier segment: each element
-                // is held against the running maximum of the elements before it
-                float run = -INFINITY;
-#pragma unroll
-                for (int e = 0; e < EPL; e++) { the[e] = run; run = fmaxf(run, v[e]); }
-                float x = run;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const float y = __shfl_up_sync(0xffffffffu, x, o);
-                    if (lane >= o) x = fmaxf(x, y);
-                }
-                float before = __shfl_up_sync(0xffffffffu, x, 1);
-                if (lane == 0) before = -INFINITY;
-#pragma unroll
-                for (int e = 0; e < EPL; e++) the[e] = fmaxf(before, the[e]);
-                // the largest running maximum used (that of the segment's last element)
-                lbmax = fmaxf(lbmax, __shfl_sync(0xffffffffu, the[EPL - 1], 31));
-#pragma unroll
-                for (int e = 0; e < EPL; e++) the[e] = __fsub_rn(the[e], kSigGap);
-            }
-            unsigned keep = 0;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) {
-                const bool k = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
-                keep |= (k ? 1u : 0u) << e;
-            }
-            const int cnt = __popc(keep);
-            int incl = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            const int tot = __shfl_sync(0xffffffffu, incl, 31);
-            int base = 0;
-            if (lane == 0) base = atomicAdd(&sh.nst, tot);
-            base = __shfl_sync(0xffffffffu, base, 0);
-            if (base + tot <= scap) {
-                int pos = base + incl - cnt;
-#pragma unroll
-                for (int e = 0; e < EPL; e++) {
-                    if ((keep >> e) & 1u) {
-                        st_t[pos] = v[e];
-                        st_i[pos] = g * SEG + lane * EPL + e;
-                        pos++;
-                    }
-                }
-            } else if (lane == 0) {
-                sh.ovf = 1;
-            }
-        }
-        if (lane == 0) atomicMax(&pubr[j], fkey(rmax));
     }
-    if (!greedy && lane == 0) atomicMax(&sh.maxlb, fkey(lbmax));
     __syncthreads();
     float lm = -INFINITY;
     for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
@@ -1395,13 +1276,7 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
 
     // ---- hand over to the finishing pass
     for (int g = tid; g < nseg; g += kRowThreads) scr.segm[(size_t)row * scr.seg_stride + g] = segm[g];
-    if (tid == 0) {
-        int* m = scr.meta + (size_t)row * 4;
-        m[0] = sh.nst;
-        m[1] = sh.ovf;
-        m[2] = (int)sh.maxlb;
-        m[3] = 0;
-    }
+    stamp(11);
 }
 
 // Finishing pass (non-greedy rows): the exact softmax denominator, the
@@ -1416,6 +1291,7 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
                   ExpFix fx, int ccap, int scap, RowScratch scr, long long* __restrict__ phase_cycles) {
     constexpr int EPL = Elem<T>::kPerLane;
     constexpr int SEG = 32 * EPL;
+    constexpr int U = kRowRound / kRowWarps;  // gathered segments in flight per warp
     const int row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const RowSmem L(V, SEG, win.window, ccap, scap);
@@ -1446,34 +1322,21 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     stamp(10);
     const float inv = __fdiv_rn(1.0f, prm.temperature);
 
-    // ---- what the streaming pass left: segment maxima, the window's
-    // overrides, the stash (each segment's start and count rebuilt here)
-    const int* meta = scr.meta + (size_t)row * 4;
-    const int nst_in = meta[0], ovf_in = meta[1];
-    const uint32_t maxlb_in = (uint32_t)meta[2];
+    // ---- what the streaming pass left: segment maxima; the window's
+    // overrides from the tables it wrote
     const int nov = (win.ov_n && win.ov_idx) ? win.ov_n[row] : 0;
     for (int g = tid; g < nseg; g += kRowThreads) {
         segm[g] = scr.segm[(size_t)row * scr.seg_stride + g];
         segov[g] = 0;
         scnt[g] = 0;
-        sstart[g] = 0x7fffffff;
     }
-    if (tid == 0) { sh.nst = nst_in; sh.ovf = ovf_in; sh.maxlb = maxlb_in; }
+    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.nhot = 0; sh.maxlb = fkey(-INFINITY); }
     __syncthreads();
     for (int j = tid; j < nov; j += kRowThreads) {
         const int q = win.ov_idx[(size_t)row * win.ov_stride + j];
         ovi[j] = q;
         ovv[j] = win.ov_val[(size_t)row * win.ov_stride + j];
         segov[q / SEG] = 1;
-    }
-    if (!ovf_in) {
-        for (int i = tid; i < nst_in; i += kRowThreads) {
-            const int q = scr.st_i[(size_t)row * scap + i];
-            st_t[i] = scr.st_t[(size_t)row * scap + i];
-            st_i[i] = q;
-            atomicAdd(&scnt[q / SEG], 1);
-            atomicMin(&sstart[q / SEG], i);
-        }
     }
     __syncthreads();
     RowView<T> rv;
@@ -1487,6 +1350,124 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     float lm = -INFINITY;
     for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
     const float maxl = rblock_max(lm, sh.red_f);
+
+    // ---- the stash: every element that may be significant for the softmax
+    // sum, t >= pre - 17.5 where pre is the maximum t before it (the exact
+    // maximum of the segments before its segment; in the first segment, of
+    // the elements before it).  A segment is gathered when its maximum
+    // reaches its threshold; the gathered segments are re-read U at a time
+    // per warp, all U loads in flight together.
+    float* pre = reinterpret_cast<float*>(segk);  // exclusive prefix maximum of t per segment (segk is set later)
+    __syncthreads();                              // red_f is free again
+    {
+        // block-wide exclusive max-scan over the segments, per thread a run
+        const int per = (nseg + kRowThreads - 1) / kRowThreads;
+        const int c0 = min(tid * per, nseg), c1 = min(c0 + per, nseg);
+        float m = -INFINITY;
+        for (int g = c0; g < c1; g++) m = fmaxf(m, __fmul_rn(segm[g], inv));
+        float x = m;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x = fmaxf(x, y);
+        }
+        if (lane == 31) sh.red_f[warp] = x;
+        __syncthreads();
+        float wpre = -INFINITY;
+        for (int w = 0; w < warp; w++) wpre = fmaxf(wpre, sh.red_f[w]);
+        float ex = __shfl_up_sync(0xffffffffu, x, 1);
+        if (lane == 0) ex = -INFINITY;
+        float run = fmaxf(wpre, ex);
+        for (int g = c0; g < c1; g++) {
+            pre[g] = run;
+            run = fmaxf(run, __fmul_rn(segm[g], inv));
+        }
+        __syncthreads();
+    }
+    // the largest threshold used (+ 17.5): the stash holds every t >= lbmax - 17.5
+    float lbmax = nseg > 1 ? pre[nseg - 1] : -INFINITY;
+    int* hot = reinterpret_cast<int*>(smem + L.hotl);  // the segments to gather, in any order
+    uint4 r[U];
+    for (int g = tid; g < nseg; g += kRowThreads)
+        if (g == 0 || __fmul_rn(segm[g], inv) >= __fsub_rn(pre[g], kSigGap)) hot[atomicAdd(&sh.nhot, 1)] = g;
+    __syncthreads();
+    const int nhot = sh.nhot;
+    for (int h0 = warp; h0 < nhot; h0 += U * kRowWarps) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int h = h0 + u * kRowWarps;
+            r[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (h < nhot && rv.full(hot[h], lane)) r[u] = rv.raw(hot[h], lane);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int h = h0 + u * kRowWarps;
+            if (h >= nhot) continue;
+            const int g = hot[h];
+            if (*(volatile int*)&sh.ovf) continue;  // the dense method takes over; stop stashing
+            float v[EPL];
+            rv.widen(g, lane, rv.full(g, lane), r[u], v);
+            float the[EPL];  // each element's threshold
+            const float th = __fsub_rn(pre[g], kSigGap);
+#pragma unroll
+            for (int e = 0; e < EPL; e++) { v[e] = __fmul_rn(v[e], inv); the[e] = th; }
+            if (g == 0) {
+                // the first segment: each element against the running maximum
+                // of the elements before it
+                float run = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) { the[e] = run; run = fmaxf(run, v[e]); }
+                float x = run;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x = fmaxf(x, y);
+                }
+                float before = __shfl_up_sync(0xffffffffu, x, 1);
+                if (lane == 0) before = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) the[e] = fmaxf(before, the[e]);
+                lbmax = fmaxf(lbmax, __shfl_sync(0xffffffffu, the[EPL - 1], 31));
+#pragma unroll
+                for (int e = 0; e < EPL; e++) the[e] = __fsub_rn(the[e], kSigGap);
+            }
+            unsigned keep = 0;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const bool kk = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
+                keep |= (kk ? 1u : 0u) << e;
+            }
+            const int cnt = __popc(keep);
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const int tot = __shfl_sync(0xffffffffu, incl, 31);
+            if (tot == 0) continue;
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&sh.nst, tot);
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (base + tot <= scap) {
+                if (lane == 0) { sstart[g] = base; scnt[g] = tot; }
+                int pos = base + incl - cnt;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    if ((keep >> e) & 1u) {
+                        st_t[pos] = v[e];
+                        st_i[pos] = g * SEG + lane * EPL + e;
+                        pos++;
+                    }
+                }
+            } else if (lane == 0) {
+                sh.ovf = 1;
+            }
+        }
+    }
+    if (lane == 0) atomicMax(&sh.maxlb, fkey(lbmax));
+    __syncthreads();
+
 
     RowResult out;
     out.token = 0; out.greedy = 0; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
@@ -1692,8 +1673,8 @@ int row_kernel_ccap(int top_k, int V) {
 }
 
 // The streaming pass, then (non-greedy calls) the finishing pass.  `scr`
-// must hold `B` rows of row_scratch_seg_stride(V) segment maxima and
-// kStashCap stash entries unless the call is greedy.
+// must hold `B` rows of row_scratch_seg_stride(V) segment maxima unless the
+// call is greedy.
 template <typename T>
 cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, RowWindow win,
                               unsigned long long* rng, RowResult* res, int* slow_list,
@@ -1702,8 +1683,7 @@ cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, RowW
     const int ccap = row_kernel_ccap(prm.top_k, V);
     if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
     const bool greedy = prm.temperature < 1e-6f;
-    if (!greedy && (!scr.segm || !scr.st_t || !scr.st_i || !scr.meta ||
-                    scr.seg_stride < row_scratch_seg_stride(V)))
+    if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V)))
         return cudaErrorInvalidValue;
     const RowSmem L(V, 32 * (16 / (int)sizeof(T)), win.window, ccap, kStashCap);
     cudaError_t err = cudaFuncSetAttribute(row_stream_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
