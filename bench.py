@@ -18,9 +18,10 @@ Reported (one JSON line on rank 0):
   e2e         rows/s through the C ABI with host buffers: each step copies
               its logits, window and RNG states from pinned host memory and
               reads the tokens back.
-  roofline    the fused row kernel's algorithmic bytes per launch (the bf16
-              logits it must read, 303,872 B per row) over its average
-              launch time, against MEASURED_PEAKS.json's HBM copy bandwidth.
+  roofline    the row kernel's streaming pass: its algorithmic bytes per
+              launch (the bf16 logits it must read, 303,872 B per row) over
+              its average launch time, against MEASURED_PEAKS.json's HBM copy
+              bandwidth.
   cpu_baseline  the reference's own sampler.h (oracle/_ref, compiled from the
               reference tree) on this host's cores, on a bounded sample.
 
@@ -47,8 +48,8 @@ PARAMS = dict(temperature=0.7, topp=0.95, minp=0.1, top_k=50, repetition_penalty
 METRIC = "sampled rows/sec @V=151936 (B=1/64/1024), % of HBM roofline, 1/2/4/8 GPU"
 WORKLOAD = ("top-k sampling, bf16 logits 4*Gumbel+U[-8,8] per row, V=151936, 1024 rows/GPU, "
             "64-token uniform window, T=0.7 k=50 p=0.95 min-p=0.1 rep=1.15")
-ROW_BYTES = V * 2            # logits the row kernel must read per row (bf16)
-STEP_ROW_BYTES = V * 2 + WINDOW * 4   # plus the window ids (penalty kernel)
+ROW_BYTES = V * 2            # logits the streaming pass must read per row (bf16)
+STEP_ROW_BYTES = V * 2 + WINDOW * 4   # plus the window ids
 
 
 def peaks():
@@ -377,11 +378,11 @@ def main():
     sync_all()
     pr = s.profile_read()
     s.profile(False)
-    row_ms = pr["row_ms"] / max(pr["row_launches"], 1)
+    row_ms = pr["stream_ms"] / max(pr["row_launches"], 1)  # the streaming pass: every logit once
     hbm, peak_kind = peaks()
     achieved = B * ROW_BYTES / (row_ms / 1e3) / 1e9
     traffic = None
-    tfile = os.path.join(ROOT, "profiles", "row_kernel_topk_bf16.txt")
+    tfile = os.path.join(ROOT, "profiles", "row_stream_kernel_topk_bf16.txt")
     if os.path.exists(tfile):
         for ln in open(tfile):
             if ln.startswith("dram_bytes_per_launch_B1024:"):
@@ -459,10 +460,10 @@ def main():
         "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic,
-                     "kernel": "qs::row_kernel<bf16>", "kernel_ms": row_ms,
+                     "kernel": "qs::row_stream_kernel<bf16>", "kernel_ms": row_ms,
                      "algorithmic_bytes_per_launch": B * ROW_BYTES, "peak_source": peak_kind,
                      "step_hbm_frac": world * B * STEP_ROW_BYTES / (ms_step / 1e3) / 1e9 / hbm / world},
-        "kernel_ms_per_step": {k: pr[k] / args.steps for k in ("penalty_ms", "row_ms", "ties_ms", "emit_ms")},
+        "kernel_ms_per_step": {k: pr[k] / args.steps for k in ("stream_ms", "finish_ms", "ties_ms", "emit_ms")},
         "cpu_baseline": cpu,
         "lm_head": lmh,
         "clocks": clk.summary(),

@@ -160,13 +160,13 @@ QS_API int qs_sample_host(qs_sampler* s, const float* h_logits, int batch, int* 
  * kernel and the launch counts since the last qs_profile_reset.  Launch
  * counts are kept whether or not profiling is on. */
 typedef struct {
-    double penalty_ms;   /* override-table kernel */
-    double row_ms;       /* fused row kernel (the HBM stream) */
-    double ties_ms;      /* exact tie-arrangement kernel */
+    double stream_ms;    /* row kernel, streaming pass (the HBM stream; window penalties) */
+    double finish_ms;    /* row kernel, finishing pass (exact sum, candidates, draw) */
+    double ties_ms;      /* exact passes: tie replay or full sort */
     double emit_ms;      /* token copy-out / history update */
     long long calls;     /* sampling calls */
-    long long launches;  /* kernels launched by this library */
-    long long row_launches;
+    long long launches;  /* kernel launch sites passed by this library's calls */
+    long long row_launches; /* streaming-pass launches */
     long long timed_calls; /* calls whose kernels were timed */
 } qs_profile;
 

@@ -49,7 +49,7 @@ class RowDebug(C.Structure):
 
 
 class Profile(C.Structure):
-    _fields_ = [("penalty_ms", C.c_double), ("row_ms", C.c_double), ("ties_ms", C.c_double),
+    _fields_ = [("stream_ms", C.c_double), ("finish_ms", C.c_double), ("ties_ms", C.c_double),
                 ("emit_ms", C.c_double), ("calls", C.c_longlong), ("launches", C.c_longlong),
                 ("row_launches", C.c_longlong), ("timed_calls", C.c_longlong)]
 

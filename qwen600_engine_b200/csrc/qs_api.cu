@@ -20,9 +20,12 @@
 namespace qs {
 
 template <typename T>
-cudaError_t launch_row_kernel(const T*, int, int, RowParams, RowWindow, unsigned long long*,
-                              RowResult*, int*, int*, int*, float*, int, ExpFix, RowScratch,
+cudaError_t launch_row_stream(const T*, int, int, RowParams, RowWindow, RowResult*, RowScratch,
                               cudaStream_t, long long* phase_cycles = nullptr);
+template <typename T>
+cudaError_t launch_row_finish(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*,
+                              int*, int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t,
+                              long long* phase_cycles = nullptr);
 cudaError_t launch_write_penalized(float*, int, int, const int*, const int*, const float*, int,
                                    cudaStream_t);
 template <typename T>
@@ -141,7 +144,7 @@ struct KernelScope {
     cudaEvent_t a = nullptr;
     KernelScope(qs_sampler* s_, int kind_, cudaStream_t st_) : s(s_), kind(kind_), st(st_) {
         s->prof.launches++;
-        if (kind == 1) s->prof.row_launches++;
+        if (kind == 0) s->prof.row_launches++;
         if (s->profiling) {
             a = take_event(s);
             cudaEventRecord(a, st);
@@ -439,13 +442,21 @@ static int run(qs_sampler* s, const Call& c) {
     CK(cudaMemsetAsync(s->slow_count, 0, sizeof(int), c.stream));
     RowParams rp{p.temperature, p.topp, p.minp, p.top_k, c.flags};
     {
+    KernelScope ks(s, 0, c.stream);
+    if (c.dtype == QS_F32)
+        CK(launch_row_stream<float>((const float*)c.logits, B, V, rp, win, s->res, s->scratch(), c.stream));
+    else
+        CK(launch_row_stream<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, s->res,
+                                            s->scratch(), c.stream));
+    }
+    if (!greedy) {
     KernelScope ks(s, 1, c.stream);
     if (c.dtype == QS_F32) {
-        CK(launch_row_kernel<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res,
+        CK(launch_row_finish<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res,
                                     s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
                                     c.cand_cap, s->fix(), s->scratch(), c.stream));
     } else {
-        CK(launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng,
+        CK(launch_row_finish<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng,
                                             s->res, s->slow_list, s->slow_count, c.cand_index,
                                             c.cand_prob, c.cand_cap, s->fix(), s->scratch(), c.stream));
     }
@@ -586,7 +597,7 @@ int qs_profile_read(qs_sampler* s, qs_profile* out) {
         CK(cudaEventSynchronize(t.b));
         float ms = 0.f;
         CK(cudaEventElapsedTime(&ms, t.a, t.b));
-        double* dst = t.kind == 0 ? &s->prof.penalty_ms : t.kind == 1 ? &s->prof.row_ms
+        double* dst = t.kind == 0 ? &s->prof.stream_ms : t.kind == 1 ? &s->prof.finish_ms
                     : t.kind == 2 ? &s->prof.ties_ms : &s->prof.emit_ms;
         if (t.kind != 4) *dst += ms;
         s->event_pool.push_back(t.a);

@@ -1672,34 +1672,54 @@ int row_kernel_ccap(int top_k, int V) {
     return c;
 }
 
-// The streaming pass, then (non-greedy calls) the finishing pass.  `scr`
-// must hold `B` rows of row_scratch_seg_stride(V) segment maxima unless the
-// call is greedy.
+// The streaming pass (every call) and the finishing pass (non-greedy
+// calls), launched separately so callers can time them apart.  `scr` must
+// hold `B` rows of row_scratch_seg_stride(V) segment maxima unless the call
+// is greedy.
 template <typename T>
-cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, RowWindow win,
-                              unsigned long long* rng, RowResult* res, int* slow_list,
-                              int* slow_count, int* cand_index, float* cand_prob, int cand_cap,
-                              ExpFix fx, RowScratch scr, cudaStream_t stream, long long* phase_cycles) {
+cudaError_t launch_row_stream(const T* logits, int B, int V, RowParams prm, RowWindow win, RowResult* res,
+                              RowScratch scr, cudaStream_t stream, long long* phase_cycles) {
     const int ccap = row_kernel_ccap(prm.top_k, V);
     if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
     const bool greedy = prm.temperature < 1e-6f;
-    if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V)))
-        return cudaErrorInvalidValue;
+    if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V))) return cudaErrorInvalidValue;
     const RowSmem L(V, 32 * (16 / (int)sizeof(T)), win.window, ccap, kStashCap);
     cudaError_t err = cudaFuncSetAttribute(row_stream_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)L.region);
     if (err != cudaSuccess) return err;
     row_stream_kernel<T><<<B, kRowThreads, L.region, stream>>>(logits, V, prm, win, res, scr, ccap,
                                                                kStashCap, phase_cycles);
-    err = cudaGetLastError();
-    if (err != cudaSuccess || greedy) return err;
-    err = cudaFuncSetAttribute(row_finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)L.total);
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_row_finish(const T* logits, int B, int V, RowParams prm, RowWindow win,
+                              unsigned long long* rng, RowResult* res, int* slow_list, int* slow_count,
+                              int* cand_index, float* cand_prob, int cand_cap, ExpFix fx, RowScratch scr,
+                              cudaStream_t stream, long long* phase_cycles) {
+    const int ccap = row_kernel_ccap(prm.top_k, V);
+    if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
+    if (prm.temperature < 1e-6f) return cudaSuccess;  // greedy rows are finished by the streaming pass
+    if (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V)) return cudaErrorInvalidValue;
+    const RowSmem L(V, 32 * (16 / (int)sizeof(T)), win.window, ccap, kStashCap);
+    cudaError_t err = cudaFuncSetAttribute(row_finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)L.total);
     if (err != cudaSuccess) return err;
     row_finish_kernel<T><<<B, kRowThreads, L.total, stream>>>(logits, V, prm, win, rng, res, slow_list,
                                                               slow_count, cand_index, cand_prob, cand_cap,
                                                               fx, ccap, kStashCap, scr, phase_cycles);
     return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, RowWindow win,
+                              unsigned long long* rng, RowResult* res, int* slow_list,
+                              int* slow_count, int* cand_index, float* cand_prob, int cand_cap,
+                              ExpFix fx, RowScratch scr, cudaStream_t stream, long long* phase_cycles) {
+    cudaError_t err = launch_row_stream<T>(logits, B, V, prm, win, res, scr, stream, phase_cycles);
+    if (err != cudaSuccess) return err;
+    return launch_row_finish<T>(logits, B, V, prm, win, rng, res, slow_list, slow_count, cand_index,
+                                cand_prob, cand_cap, fx, scr, stream, phase_cycles);
 }
 
 template cudaError_t launch_row_kernel<float>(const float*, int, int, RowParams, RowWindow,
@@ -1709,6 +1729,17 @@ template cudaError_t launch_row_kernel<__nv_bfloat16>(const __nv_bfloat16*, int,
                                                       RowWindow, unsigned long long*, RowResult*,
                                                       int*, int*, int*, float*, int, ExpFix, RowScratch,
                                                       cudaStream_t, long long*);
+template cudaError_t launch_row_stream<float>(const float*, int, int, RowParams, RowWindow, RowResult*,
+                                              RowScratch, cudaStream_t, long long*);
+template cudaError_t launch_row_stream<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
+                                                      RowResult*, RowScratch, cudaStream_t, long long*);
+template cudaError_t launch_row_finish<float>(const float*, int, int, RowParams, RowWindow,
+                                              unsigned long long*, RowResult*, int*, int*, int*, float*,
+                                              int, ExpFix, RowScratch, cudaStream_t, long long*);
+template cudaError_t launch_row_finish<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
+                                                      unsigned long long*, RowResult*, int*, int*, int*,
+                                                      float*, int, ExpFix, RowScratch, cudaStream_t,
+                                                      long long*);
 
 // QS_FLAG_WRITE_PENALIZED: the reference's in-place penalty update of fp32
 // logits (sampler.h:114-141), written after every pass has read the raw row.
