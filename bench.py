@@ -398,19 +398,12 @@ def main():
         h_hist, h_counts, h_count = hist.cpu().pin_memory(), counts.cpu().pin_memory(), count.cpu().pin_memory()
         h_rng = rng.cpu().pin_memory()
         h_tok = torch.empty(B, dtype=torch.int32).pin_memory()
-        d_logits = torch.empty_like(bufs[0][0])
-        d_hist, d_counts, d_count = torch.empty_like(hist), torch.empty_like(counts), torch.empty_like(count)
-        d_rng = torch.empty_like(rng)
-        d_tok = torch.empty(B, dtype=torch.int32, device=dev)
 
         def e2e_step(i):
-            d_logits.copy_(h_logits[i % 2], non_blocking=True)
-            d_hist.copy_(h_hist, non_blocking=True)
-            d_counts.copy_(h_counts, non_blocking=True)
-            d_count.copy_(h_count, non_blocking=True)
-            d_rng.copy_(h_rng, non_blocking=True)
-            s.sample_rows(d_logits, d_hist, d_counts, d_count, d_rng, out=d_tok)
-            h_tok.copy_(d_tok, non_blocking=True)
+            # the C ABI's host-buffer entry: logits, window and RNG states in,
+            # tokens and advanced states out, all through host memory
+            s.sample_rows_host(h_logits[i % 2], h_hist, h_counts, h_count, h_rng, out=h_tok,
+                               stream=main_stream, synchronize=False)
 
         e2e_step(0)
         sync_all()
@@ -427,8 +420,9 @@ def main():
         h2d = (bufs[0][0].numel() * 2 + hist.numel() * 4 + counts.numel() * 4 + count.numel() * 4
                + rng.numel() * 8)
         e2e = {"value": world * B / (ems / args.e2e_steps / 1e3), "unit": "rows/s",
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(B * 4),
-               "steps": args.e2e_steps, "path": "pinned host -> qs_sample_rows (C ABI) -> host"}
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(B * (4 + 8)),
+               "steps": args.e2e_steps,
+               "path": "pinned host -> qs_sample_rows_host (C ABI; tokens and RNG states back) -> host"}
 
     # ---- the decode tail (final RMSNorm + lm_head, SURVEY configuration 5):
     # 128 hidden rows x W [151936, 1024] bf16, two weight copies used in turn

@@ -154,6 +154,18 @@ QS_API int qs_sample_rows_debug(qs_sampler* s, const void* d_logits, qs_dtype dt
 QS_API int qs_sample_host(qs_sampler* s, const float* h_logits, int batch, int* h_tokens,
                    unsigned flags);
 
+/* qs_sample_rows with every buffer on the host (the reference's sample()
+ * takes host logits, sampler.h:165; page-locked buffers copy fastest):
+ * h_logits [batch, vocab] of `dtype`, the caller's window as in
+ * qs_sample_rows, h_rng [batch] states advanced in place, h_tokens [batch].
+ * Enqueued on `stream` (logits staged in chunks over the handle's copy
+ * streams); the outputs are valid once the stream has run.  The handle's own
+ * history and RNG states are untouched. */
+QS_API int qs_sample_rows_host(qs_sampler* s, const void* h_logits, qs_dtype dtype, int batch,
+                               int vocab, const int* h_hist, const float* h_hist_counts,
+                               const int* h_hist_count, int window, unsigned long long* h_rng,
+                               int* h_tokens, void* stream, unsigned flags);
+
 /* Kernel timing for benchmarks.  With profiling on, every sampling call
  * records CUDA events around each of its kernels on the caller's stream;
  * qs_profile_read waits for them and returns the accumulated device time per

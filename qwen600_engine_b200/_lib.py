@@ -28,7 +28,7 @@ QS_FLAG_INDEX_TIES = 2
 EXPORTS = (
     "qs_build_sampler", "qs_free_sampler", "qs_set_params", "qs_get_params",
     "qs_set_rng_state", "qs_get_rng_state", "qs_reset_sampler_history", "qs_sample",
-    "qs_sample_rows", "qs_sample_rows_debug", "qs_sample_host", "qs_last_error",
+    "qs_sample_rows", "qs_sample_rows_debug", "qs_sample_host", "qs_sample_rows_host", "qs_last_error",
     "qs_max_vocab", "qs_profile_enable", "qs_profile_reset", "qs_profile_read",
     "qs_argmax_rows_static", "qs_lm_head", "qs_lm_head_sample", "qs_lm_head_logits",
     "qs_lm_head_status",
@@ -83,6 +83,7 @@ def _load() -> C.CDLL:
     lib.qs_sample_rows_debug.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, vp, vp,
                                          vp, vp, vp, i32, vp, u32]
     lib.qs_sample_host.argtypes = [vp, vp, i32, vp, u32]
+    lib.qs_sample_rows_host.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, vp, vp, u32]
     lib.qs_profile_enable.argtypes = [vp, i32]
     lib.qs_profile_reset.argtypes = [vp]
     lib.qs_profile_read.argtypes = [vp, P(Profile)]

@@ -171,6 +171,30 @@ class Sampler:
                                       int(flags)))
         return out
 
+    def sample_rows_host(self, logits, hist=None, hist_counts=None, hist_count=None, rng=None,
+                         out=None, *, flags: int = 0, stream=None, synchronize: bool = True):
+        """sample_rows with host (CPU, ideally pinned) tensors: logits [B, V]
+        float32/bfloat16, the caller's window, rng int64 [B] (advanced in
+        place); returns int32 tokens [B] on the host.  The copies and the
+        sampling are enqueued on ``stream``; with ``synchronize`` the call
+        waits for them."""
+        torch = _torch()
+        x = logits if logits.dim() == 2 else logits.view(1, -1)
+        if x.is_cuda or not x.is_contiguous():
+            raise SamplerError(_lib.QS_ERR_INVALID, "logits must be a contiguous host tensor")
+        if rng is None or rng.is_cuda:
+            raise SamplerError(_lib.QS_ERR_INVALID, "rng states must be a host tensor (int64 [B])")
+        B, V = int(x.shape[0]), int(x.shape[1])
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32)
+        W = 0 if hist is None else int(hist.shape[1])
+        check(_lib.lib.qs_sample_rows_host(
+            self._h, _ptr(x), _dtype_code(x), B, V, _ptr(hist), _ptr(hist_counts), _ptr(hist_count), W,
+            _ptr(rng), _ptr(out), _stream_handle(stream), int(flags)))
+        if synchronize:
+            (stream if stream is not None else torch.cuda.current_stream()).synchronize()
+        return out
+
     def sample_rows(self, logits, hist=None, hist_counts=None, hist_count=None, rng=None,
                     out=None, *, debug: bool = False, probs: bool = False, cand_cap: int = 0,
                     flags: int = 0, stream=None):
