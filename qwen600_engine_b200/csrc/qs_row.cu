@@ -1392,6 +1392,10 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         if (g == 0 || __fmul_rn(segm[g], inv) >= __fsub_rn(pre[g], kSigGap)) hot[atomicAdd(&sh.nhot, 1)] = g;
     __syncthreads();
     const int nhot = sh.nhot;
+    // every gathered segment's lines requested into L2 at once (4 per segment),
+    // so the gather's batches after the first find them there
+    for (int q = tid; q < 4 * nhot; q += kRowThreads)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(rv.L + (size_t)hot[q >> 2] * SEG) + (q & 3) * 128));
     for (int h0 = warp; h0 < nhot; h0 += U * kRowWarps) {
 #pragma unroll
         for (int u = 0; u < U; u++) {
@@ -1437,21 +1441,23 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
                 const bool kk = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
                 keep |= (kk ? 1u : 0u) << e;
             }
-            const int cnt = __popc(keep);
-            int incl = cnt;
+            // the kept elements' places in index order: one ballot per slot of
+            // the lanes' vectors (independent, no scan chain)
+            const unsigned lt = (1u << lane) - 1u;
+            int before = 0, tot = 0;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
+            for (int e = 0; e < EPL; e++) {
+                const unsigned be = __ballot_sync(0xffffffffu, (keep >> e) & 1u);
+                before += __popc(be & lt);
+                tot += __popc(be);
             }
-            const int tot = __shfl_sync(0xffffffffu, incl, 31);
             if (tot == 0) continue;
             int base = 0;
             if (lane == 0) base = atomicAdd(&sh.nst, tot);
             base = __shfl_sync(0xffffffffu, base, 0);
             if (base + tot <= scap) {
                 if (lane == 0) { sstart[g] = base; scnt[g] = tot; }
-                int pos = base + incl - cnt;
+                int pos = base + before;
 #pragma unroll
                 for (int e = 0; e < EPL; e++) {
                     if ((keep >> e) & 1u) {
