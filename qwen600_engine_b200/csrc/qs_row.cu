@@ -204,9 +204,9 @@ struct RowView {
     __device__ __forceinline__ uint4 raw(int g, int lane) const {
         return __ldg(reinterpret_cast<const uint4*>(L + g * SEG + lane * EPL));
     }
-    // Lane's EPL penalised logits of segment g (out-of-row slots are -inf).
-    __device__ __forceinline__ void widen(int g, int lane, bool is_full, const uint4& r,
-                                          float* v) const {
+    // Lane's EPL raw logits of segment g (out-of-row slots are -inf).
+    __device__ __forceinline__ void widen_raw(int g, int lane, bool is_full, const uint4& r,
+                                              float* v) const {
         const int base = g * SEG + lane * EPL;
         if (is_full) {
             if constexpr (EPL == 8) {
@@ -225,6 +225,12 @@ struct RowView {
             for (int e = 0; e < EPL; e++)
                 v[e] = (base + e < V) ? Elem<T>::widen(L[base + e]) : -INFINITY;
         }
+    }
+    // Lane's EPL penalised logits of segment g (out-of-row slots are -inf).
+    __device__ __forceinline__ void widen(int g, int lane, bool is_full, const uint4& r,
+                                          float* v) const {
+        const int base = g * SEG + lane * EPL;
+        widen_raw(g, lane, is_full, r, v);
         if (segov[g]) {
             int lo = 0, hi = nov;  // first window token >= base
             while (lo < hi) { int m = (lo + hi) >> 1; if (ovi[m] < base) lo = m + 1; else hi = m; }
@@ -479,6 +485,7 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
 struct RowSmem {
     size_t segm, segk, segov, ovi, ovv, ofirst, pairs, pcnt, pubr, hotl, region, ct, ci, cp, so, ck,
         rhist, total;
+    size_t segf, rawv, plv, stream_total;  // streaming pass only (overlays the finishing pass's region)
     int nseg, nrounds, scap, ccap, npairs;
     __host__ __device__ static size_t r16(size_t b) { return (b + 15) & ~(size_t)15; }
     __host__ __device__ RowSmem(int V, int seg, int ov_stride, int ccap_, int scap_) {
@@ -511,6 +518,11 @@ struct RowSmem {
         ck = p; p += r16(8 * (size_t)ccap);
         rhist = p; p += r16(4 * 256);
         total = p;
+        p = region;
+        segf = p; p += r16(4 * (size_t)nseg);
+        rawv = p; p += r16(4 * ovs);
+        plv = p; p += r16(4 * ovs);
+        stream_total = p;
     }
 };
 
@@ -1073,6 +1085,9 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     unsigned long long* pairs = (unsigned long long*)(smem + L.pairs);
     float* pcnt = (float*)(smem + L.pcnt);
     uint32_t* pubr = (uint32_t*)(smem + L.pubr);      // per streaming round: max key seen
+    int* segf = (int*)(smem + L.segf);                // first window token of a marked segment
+    float* rawv = (float*)(smem + L.rawv);            // window tokens' raw logits, as streamed
+    float* plv = (float*)(smem + L.plv);              // max of the other elements of the token's lane
     __shared__ RowShared sh;
 
     long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
@@ -1171,26 +1186,12 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         }
         nov = tot;
         __syncthreads();
-        const int nv = sh.misc[7];
-        // each window token's penalised value from its raw logit, replaying
-        // its occurrences in slot order
-        const T* Lrow = logits + (size_t)row * V;
+        // mark the segments holding window tokens; the penalised values are
+        // formed after the streaming pass from the raw logits it captures
         for (int j = tid; j < nov; j += kRowThreads) {
-            const int t = ovi[j];
-            const int q1 = (j + 1 < nov) ? ofirst[j + 1] : nv;
-            float x = Elem<T>::widen(Lrow[t]);
-            for (int q = ofirst[j]; q < q1; q++) {
-                if (win.rp != 1.0f) x = (x > 0.0f) ? __fdiv_rn(x, win.rp) : __fmul_rn(x, win.rp);
-                if (win.fp != 0.0f)
-                    x = __fsub_rn(x, __fmul_rn(win.fp, pcnt[(int)(pairs[q] & 0xFFFFFFFFull)]));
-                if (win.pp != 0.0f) x = __fsub_rn(x, win.pp);
-            }
-            ovv[j] = x;
-            segov[t / SEG] = 1;
-            if (win.ov_idx) {
-                win.ov_idx[(size_t)row * win.ov_stride + j] = t;
-                win.ov_val[(size_t)row * win.ov_stride + j] = x;
-            }
+            const int g = ovi[j] / SEG;
+            segov[g] = 1;
+            if (j == 0 || ovi[j - 1] / SEG != g) segf[g] = j;
         }
     }
     if (tid == 0 && win.ov_n) win.ov_n[row] = nov;
@@ -1221,23 +1222,94 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
             const int u = __ffs(slow) - 1;
             slow &= slow - 1;
             const int g = g0 + u * kRowWarps;
-            // the segment's vector is still in r[u] (partial lanes and window
-            // tokens are resolved by widen)
+            // the segment's vector is still in r[u]; partial lanes read -inf
+            // past the row
             uint4 ru = r[0];
 #pragma unroll
             for (int q = 1; q < U; q++)
                 if (q == u) ru = r[q];
             float v[EPL];
-            rv.widen(g, lane, rv.full(g, lane), ru, v);
-            float m = v[0];
+            rv.widen_raw(g, lane, rv.full(g, lane), ru, v);
+            // Window tokens are left out here.  A lane holding one records the
+            // token's raw logit and the fmaxf of its other elements (from a NaN
+            // start, fmaxf's identity), and offers the smallest order key; the
+            // fold after the penalties are replayed completes its maximum.
+            const int base = g * SEG + lane * EPL;
+            uint32_t own = 0;
+            int k0 = 0, k1 = 0;
+            if (segov[g]) {
+                k0 = segf[g];
+                k1 = k0;
+                while (k1 < nov && ovi[k1] < (g + 1) * SEG) {
+                    const int p = ovi[k1] - base;
+                    if (p >= 0 && p < EPL) own |= 1u << p;
+                    k1++;
+                }
+            }
+            float m = __uint_as_float(0x7fffffffu);
 #pragma unroll
-            for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
-            const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
+            for (int e = 0; e < EPL; e++)
+                if (!((own >> e) & 1u)) m = fmaxf(m, v[e]);
+            if (own) {
+                for (int k = k0; k < k1; k++) {
+                    const int p = ovi[k] - base;
+                    if (p >= 0 && p < EPL) {
+                        float x = v[0];
+#pragma unroll
+                        for (int e = 1; e < EPL; e++)
+                            if (e == p) x = v[e];
+                        rawv[k] = x;
+                        plv[k] = m;
+                    }
+                }
+            }
+            const uint32_t km = __reduce_max_sync(0xffffffffu, own ? 0u : fkey(m));
             if (lane == 0) segm[g] = fkey_inv(km);
         }
         if (j + 1 < L.nrounds) request(j + 1);  // r is free: every maximum of this round is taken
     }
     __syncthreads();
+    if (nov > 0) {
+        // each window token's penalised value from the raw logit the pass
+        // captured, replaying its occurrences in slot order (sampler.h:114-141)
+        const int nv = sh.misc[7];
+        for (int j = tid; j < nov; j += kRowThreads) {
+            const int q1 = (j + 1 < nov) ? ofirst[j + 1] : nv;
+            float x = rawv[j];
+            for (int q = ofirst[j]; q < q1; q++) {
+                if (win.rp != 1.0f) x = (x > 0.0f) ? __fdiv_rn(x, win.rp) : __fmul_rn(x, win.rp);
+                if (win.fp != 0.0f)
+                    x = __fsub_rn(x, __fmul_rn(win.fp, pcnt[(int)(pairs[q] & 0xFFFFFFFFull)]));
+                if (win.pp != 0.0f) x = __fsub_rn(x, win.pp);
+            }
+            ovv[j] = x;
+            if (win.ov_idx) {
+                win.ov_idx[(size_t)row * win.ov_stride + j] = ovi[j];
+                win.ov_val[(size_t)row * win.ov_stride + j] = x;
+            }
+        }
+        __syncthreads();
+        // fold: per marked segment, each lane that held window tokens offers
+        // the fmaxf of its other elements and its penalised tokens, compared
+        // by order key with the rest of the segment as the warp reduction does
+        for (int j = tid; j < nov; j += kRowThreads) {
+            const int g = ovi[j] / SEG;
+            if (segf[g] != j) continue;
+            uint32_t km = fkey(segm[g]);
+            int k = j;
+            while (k < nov && ovi[k] / SEG == g) {
+                const int lk = (ovi[k] - g * SEG) / EPL;
+                float q = plv[k];
+                while (k < nov && ovi[k] / SEG == g && (ovi[k] - g * SEG) / EPL == lk) {
+                    q = fmaxf(q, ovv[k]);
+                    k++;
+                }
+                km = max(km, fkey(q));
+            }
+            segm[g] = fkey_inv(km);
+        }
+        __syncthreads();
+    }
     float lm = -INFINITY;
     for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
     const float maxl = rblock_max(lm, sh.red_f);
@@ -1691,9 +1763,9 @@ cudaError_t launch_row_stream(const T* logits, int B, int V, RowParams prm, RowW
     if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V))) return cudaErrorInvalidValue;
     const RowSmem L(V, 32 * (16 / (int)sizeof(T)), win.window, ccap, kStashCap);
     cudaError_t err = cudaFuncSetAttribute(row_stream_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)L.region);
+                                           (int)L.stream_total);
     if (err != cudaSuccess) return err;
-    row_stream_kernel<T><<<B, kRowThreads, L.region, stream>>>(logits, V, prm, win, res, scr, ccap,
+    row_stream_kernel<T><<<B, kRowThreads, L.stream_total, stream>>>(logits, V, prm, win, res, scr, ccap,
                                                                kStashCap, phase_cycles);
     return cudaGetLastError();
 }
