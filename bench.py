@@ -261,6 +261,64 @@ def measure_lm_head(torch, dev, B=128, K=1024, iters=20):
                     "path and ~16% of rows the tie-order pass"}
 
 
+def measure_lm_head_sharded(torch, dev, rank, world, B=128, K=1024, iters=20):
+    """The decode tail of configuration 5 on `world` GPUs, vocabulary-sharded
+    (shard.VocabShardedLmHead): each rank streams its slice of W, stores each
+    row's logits into the rank that samples it, then samples its row block
+    (64-token windows, temperature 0.6, top-k 20, top-p 0.95, min-p 0.05,
+    repetition penalty 1.1).  CUDA events per rank, the slowest rank's time;
+    slice copies used in turn so that together they exceed L2."""
+    from qwen600_engine_b200 import shard
+    from qwen600_engine_b200.sampler import Sampler
+    c0, n = shard.vocab_shard(rank, world, V)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    h = torch.randn((B, K), generator=g, device=dev).to(torch.bfloat16)
+    ncopy = max(2, -(-300_000_000 // (n * K * 2)))
+    gw = torch.Generator(device=dev)
+    gw.manual_seed(6 + rank)
+    ws = [(0.02 * torch.randn((n, K), generator=gw, device=dev)).to(torch.bfloat16) for _ in range(ncopy)]
+    head = shard.VocabShardedLmHead(ws[0], c0, V, B, rank=rank, world=world)
+    a_, b_ = shard.row_block(rank, world, B)
+    rows_n = b_ - a_
+    s = Sampler(0.6, 0.95, 0.05, 20, 1.1, 0.0, 0.0, 64, 1, max_batch=max(rows_n, 1), device=dev.index or 0)
+    hist = torch.randint(0, V, (max(rows_n, 1), 64), generator=g, device=dev, dtype=torch.int32)
+    cnt = torch.full((max(rows_n, 1),), 64, device=dev, dtype=torch.int32)
+    rng = torch.arange(max(rows_n, 1), device=dev, dtype=torch.int64) + 1 + a_
+    tok = torch.empty(max(rows_n, 1), dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream()
+
+    def one(i, sample):
+        rows = head(h, weight=ws[i % ncopy])
+        if sample and rows_n:
+            s.sample_rows(rows, hist[:rows_n], None, cnt[:rows_n], rng[:rows_n], out=tok[:rows_n])
+
+    res = {}
+    for sample in (False, True):
+        for i in range(3):
+            one(i, sample)
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(st)
+        for i in range(iters):
+            one(i, sample)
+        ev1.record(st)
+        torch.cuda.synchronize()
+        res[sample] = shard.max_over_ranks(1e3 * ev0.elapsed_time(ev1) / iters, device=dev)
+    head.status()
+    head.close()
+    s.free()
+    byts = V * K * 2 + B * V * 2
+    return {"config": f"hidden [{B},{K}] bf16 replicated -> RMSNorm -> W [{V},{K}] bf16 split by vocabulary "
+                      f"over {world} GPUs ({n} rows each), logits rows stored to their sampling GPU over NVLink",
+            "us_per_step": res[False], "with_sampling_us": res[True],
+            "rows_per_s_with_sampling": B / (res[True] * 1e-6),
+            "whole_job_GBps": byts / (res[False] * 1e-6) / 1e9,
+            "note": "max over ranks of CUDA-event time; the step includes the completion barrier "
+                    "(one-element NCCL all-reduce)"}
+
+
 def make_inputs(torch, B, seed, device):
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -429,6 +487,8 @@ def main():
     lmh = None
     if rank == 0 and world == 1 and args.lm_head:
         lmh = measure_lm_head(torch, dev)
+    if world > 1 and args.lm_head:
+        lmh = measure_lm_head_sharded(torch, dev, rank, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -29,6 +29,7 @@
 #ifndef QWEN600_SAMPLER_H
 #define QWEN600_SAMPLER_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -225,6 +226,39 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
 QS_API int qs_lm_head(const void* d_hidden, const void* d_norm_weight, const void* d_weight,
                       int batch, int hidden_dim, int vocab, void* d_normed, void* d_logits,
                       int* d_error_flag, void* stream);
+
+/* Vocabulary-sharded decode tail for nranks GPUs (one process each).  It
+ * replaces, for one slice of the vocabulary, the reference's lm_head GEMM
+ * (qwen_model.cuh:607-629), which has no multi-GPU form.  Every rank holds the
+ * same final hidden rows and its own slice W[col0 : col0 + shard_cols) of the
+ * tied weight; it normalises the rows as qs_lm_head does (into d_normed) and
+ * computes its slice of every row's logits.  Row b is sampled by rank
+ * b / rows_per_rank: each logit row segment is stored straight into that
+ * rank's buffer d_row_dst[rank] (bf16 [rows_per_rank, vocab], row
+ * b % rows_per_rank, columns col0 ..), over NVLink for the other ranks, so
+ * once every rank's call has completed (a barrier on the stream, e.g. a
+ * one-element NCCL all-reduce) each rank holds whole logit rows, bit-identical
+ * to qs_lm_head's, for the sampler.  d_row_dst is a host array of nranks
+ * device pointers: this rank's own buffer and the peers' buffers mapped with
+ * qs_ipc_open.  vocab, col0 and shard_cols multiples of 8; nranks <= 8;
+ * hidden_dim a multiple of 64; all buffers 16-byte aligned.  Allocates
+ * nothing.  d_error_flag as for qs_lm_head. */
+QS_API int qs_lm_head_shard(const void* d_hidden, const void* d_norm_weight, const void* d_weight_shard,
+                            int batch, int hidden_dim, int vocab, int col0, int shard_cols,
+                            void* d_normed, void* const* d_row_dst, int nranks, int rows_per_rank,
+                            int* d_error_flag, void* stream);
+
+/* Device buffers other processes on the node can map (CUDA IPC), for the row
+ * buffers of qs_lm_head_shard; no counterpart in the reference.
+ * qs_ipc_alloc allocates `bytes` on the current device and writes its
+ * handle (qs_ipc_handle_bytes() bytes) to `handle`; another process passes
+ * that handle to qs_ipc_open to get a pointer it can store to, and releases
+ * it with qs_ipc_close; the owner frees the buffer with qs_ipc_free. */
+QS_API int qs_ipc_handle_bytes(void);
+QS_API int qs_ipc_alloc(size_t bytes, void** d_ptr, void* handle);
+QS_API int qs_ipc_open(const void* handle, void** d_ptr);
+QS_API int qs_ipc_close(void* d_ptr);
+QS_API int qs_ipc_free(void* d_ptr);
 
 /* qs_lm_head into the handle's workspace followed by qs_sample on the
  * resulting bf16 logits: the reference's forward() tail plus sample()

@@ -47,6 +47,8 @@ cudaError_t launch_lm_head(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bflo
                            int, int*, cudaStream_t);
 cudaError_t launch_rmsnorm(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int,
                            cudaStream_t);
+cudaError_t launch_lm_head_shard(const __nv_bfloat16*, const __nv_bfloat16*, int, int, int, int, int*,
+                                 const LhPeer&, cudaStream_t);
 
 // host copy of the libm expf correction table (generated at build time)
 #include "qs_exp_table.inc"
@@ -715,6 +717,106 @@ int qs_lm_head(const void* d_hidden, const void* d_norm_weight, const void* d_we
     return lm_head_launch(d_hidden, d_norm_weight, d_weight, batch, hidden_dim, vocab,
                           (__nv_bfloat16*)d_normed, (__nv_bfloat16*)d_logits, err, sms,
                           (cudaStream_t)stream);
+}
+
+int qs_lm_head_shard(const void* d_hidden, const void* d_norm_weight, const void* d_weight_shard,
+                     int batch, int hidden_dim, int vocab, int col0, int shard_cols, void* d_normed,
+                     void* const* d_row_dst, int nranks, int rows_per_rank, int* d_error_flag,
+                     void* stream) {
+    g_err.clear();
+    int rc = lm_head_args(d_hidden, d_weight_shard, batch, hidden_dim, shard_cols);
+    if (rc) return rc;
+    if (vocab < 1 || vocab > kMaxVocab) return fail(QS_ERR_UNSUPPORTED, "vocab %d outside [1, %d]", vocab, kMaxVocab);
+    if (vocab % 8 || col0 % 8 || shard_cols % 8)
+        return fail(QS_ERR_UNSUPPORTED, "vocab, col0 and shard_cols must be multiples of 8");
+    if (col0 < 0 || col0 + shard_cols > vocab)
+        return fail(QS_ERR_INVALID, "shard [%d, %d) outside the vocabulary [0, %d)", col0, col0 + shard_cols, vocab);
+    if (nranks < 1 || nranks > kLhMaxRanks)
+        return fail(QS_ERR_UNSUPPORTED, "nranks %d outside [1, %d]", nranks, kLhMaxRanks);
+    if (rows_per_rank < 1 || (long long)nranks * rows_per_rank < batch)
+        return fail(QS_ERR_INVALID, "%d ranks x %d rows do not hold %d rows", nranks, rows_per_rank, batch);
+    if (!d_normed || !d_row_dst) return fail(QS_ERR_INVALID, "NULL output buffer");
+    if (((uintptr_t)d_normed) & 15) return fail(QS_ERR_INVALID, "normed must be 16-byte aligned");
+    LhPeer peer;
+    memset(&peer, 0, sizeof(peer));
+    for (int r = 0; r < nranks; r++) {
+        if (!d_row_dst[r] || (((uintptr_t)d_row_dst[r]) & 15))
+            return fail(QS_ERR_INVALID, "row buffer of rank %d is NULL or not 16-byte aligned", r);
+        peer.dst[r] = (__nv_bfloat16*)d_row_dst[r];
+    }
+    peer.nranks = nranks;
+    peer.rows_per = rows_per_rank;
+    peer.col0 = col0;
+    peer.ld = vocab;
+    int* err = d_error_flag;
+    if (!err) {
+        void* p = nullptr;
+        CK(cudaGetSymbolAddress(&p, g_lm_head_err));
+        err = (int*)p;
+    }
+    if (batch == 0) return QS_OK;
+    int dev = 0, sms = 148;
+    CK(cudaGetDevice(&dev));
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+        sms = 148;
+    cudaStream_t st = (cudaStream_t)stream;
+    __nv_bfloat16* normed = (__nv_bfloat16*)d_normed;
+    CK(launch_rmsnorm((const __nv_bfloat16*)d_hidden, (const __nv_bfloat16*)d_norm_weight, normed, batch,
+                      hidden_dim, st));
+    for (int r0 = 0; r0 < batch; r0 += 128) {
+        const int rb = batch - r0 < 128 ? batch - r0 : 128;
+        peer.row0 = r0;
+        const cudaError_t e = launch_lm_head_shard(normed + (size_t)r0 * hidden_dim,
+                                                   (const __nv_bfloat16*)d_weight_shard, rb, shard_cols,
+                                                   hidden_dim, sms, err, peer, st);
+        if (e == cudaErrorInvalidValue)
+            return fail(QS_ERR_UNSUPPORTED, "lm_head: the tensor maps of these buffers cannot be built");
+        CK(e);
+    }
+    return QS_OK;
+}
+
+int qs_ipc_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int qs_ipc_alloc(size_t bytes, void** d_ptr, void* handle) {
+    g_err.clear();
+    if (!d_ptr || !handle || bytes == 0) return fail(QS_ERR_INVALID, "NULL argument or zero size");
+    *d_ptr = nullptr;
+    void* p = nullptr;
+    CK(cudaMalloc(&p, bytes));
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(QS_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    }
+    memcpy(handle, &h, sizeof(h));
+    *d_ptr = p;
+    return QS_OK;
+}
+
+int qs_ipc_open(const void* handle, void** d_ptr) {
+    g_err.clear();
+    if (!handle || !d_ptr) return fail(QS_ERR_INVALID, "NULL argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *d_ptr = nullptr;
+    CK(cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return QS_OK;
+}
+
+int qs_ipc_close(void* d_ptr) {
+    g_err.clear();
+    if (!d_ptr) return QS_OK;
+    CK(cudaIpcCloseMemHandle(d_ptr));
+    return QS_OK;
+}
+
+int qs_ipc_free(void* d_ptr) {
+    g_err.clear();
+    if (!d_ptr) return QS_OK;
+    CK(cudaFree(d_ptr));
+    return QS_OK;
 }
 
 int qs_lm_head_sample(qs_sampler* s, const void* d_hidden, const void* d_norm_weight,

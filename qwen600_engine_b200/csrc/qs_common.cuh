@@ -37,6 +37,17 @@ constexpr int kStashCap = 1536;  // stashed elements per row before the dense me
 
 // What the row kernel's streaming pass leaves for its finishing pass, per row
 // (global memory): the penalised segment maxima.
+// Where a vocabulary-sharded launch stores its logits: batch row b (of the
+// call, counted from row0) belongs to rank (row0 + b) / rows_per and goes to
+// row (row0 + b) % rows_per of that rank's [rows_per, ld] buffer, at column
+// col0 + the tile's column.  nranks == 0: the plain [B, V] output.
+constexpr int kLhMaxRanks = 8;
+struct LhPeer {
+    __nv_bfloat16* dst[kLhMaxRanks];
+    int nranks, rows_per, row0, col0;
+    long long ld;
+};
+
 struct RowScratch {
     float* segm;   // [rows][seg_stride]
     int seg_stride;

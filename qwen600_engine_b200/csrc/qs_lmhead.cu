@@ -11,14 +11,16 @@
 // (qwen_model.cuh:607-629: bf16 inputs and output, fp32 compute).  It is a
 // persistent, warp-specialised tcgen05 GEMM:
 //   warp 0  one thread issues TMA loads (128B-swizzled K-major tiles of the
-//           normed hidden rows and of 208 vocabulary rows of W) into a
-//           5-stage shared-memory ring;
-//   warp 1  one thread issues tcgen05.mma (M = 128 batch rows, N = 208
+//           normed hidden rows and of N vocabulary rows of W) into a
+//           4-stage shared-memory ring;
+//   warp 1  one thread issues tcgen05.mma (M = 128 batch rows, N = 128..208
 //           vocabulary rows, K = 16 per instruction) into one of two TMEM
 //           accumulators, and tcgen05.commit frees each stage and hands
 //           a finished accumulator to the epilogue;
 //   warps 2-5 read the accumulator with tcgen05.ld (each warp its 32 TMEM
-//           lanes = 32 batch rows), round to bf16 and store the logits.
+//           lanes = 32 batch rows), round to bf16 and store the logits:
+//           to [B, V], or, for a vocabulary-sharded launch, each row to the
+//           buffer of the GPU that samples it (peer stores over NVLink).
 // W is read from HBM exactly once per launch (311 MB for Qwen3-0.6B: the
 // bound); the hidden rows (at most 256 KB) are re-read from L2 per tile.
 // Every wait is bounded: after kLhWaitNs the kernel raises an error flag,
@@ -34,23 +36,13 @@
 namespace qs {
 
 constexpr int kLhM = 128;                       // batch rows per launch (MMA M)
-constexpr int kLhN = 208;                       // vocabulary rows per tile (MMA N): 731 tiles of
-                                                // Qwen3's 151,936 rows spread over 148 SMs
-                                                // within 1.2% of evenly
 constexpr int kLhK = 64;                        // K per stage: one 128-byte swizzle row
 constexpr int kLhStages = 4;
-constexpr uint32_t kLhOutTile = 32 * kLhN * 2;   // one epilogue warp's bf16 rows of a tile
 constexpr int kLhThreads = 192;
 constexpr uint32_t kLhStageA = kLhM * kLhK * 2;  // 16 KB
-constexpr uint32_t kLhStageB = kLhN * kLhK * 2;  // 26 KB
 constexpr uint32_t kLhAccStride = 256;           // TMEM columns between the two accumulators
 constexpr uint32_t kLhTmemCols = 2 * kLhAccStride;
 constexpr unsigned long long kLhWaitNs = 2000000000ull;
-
-// tcgen05.mma kind::f16 instruction descriptor: fp32 accumulator, bf16 A and
-// B, both K-major, N = kLhN, M = 128.
-constexpr uint32_t kLhIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kLhN >> 3) << 17) |
-                              ((uint32_t)(kLhM >> 4) << 24);
 
 struct LhShared {
     unsigned long long full[kLhStages];
@@ -61,9 +53,23 @@ struct LhShared {
     int abort;
 };
 
-size_t lm_head_smem() {
-    return 1024 + kLhStages * (size_t)(kLhStageA + kLhStageB) + 4 * (size_t)kLhOutTile + sizeof(LhShared);
-}
+// Vocabulary rows per tile (MMA N, a multiple of 16 up to 256), chosen per
+// launch so the tiles spread evenly over the SMs: 208 for Qwen3's 151,936
+// rows on one GPU (731 tiles over 148 SMs within 1.2% of evenly), narrower
+// tiles for the slices of a vocabulary-sharded launch.
+template <int N>
+struct LhTile {
+    static_assert(N % 16 == 0 && N >= 16 && N <= 256, "MMA N");
+    static constexpr uint32_t kStageB = N * kLhK * 2;
+    static constexpr uint32_t kOutTile = 32 * N * 2;  // one epilogue warp's bf16 rows of a tile
+    // tcgen05.mma kind::f16 instruction descriptor: fp32 accumulator, bf16 A
+    // and B, both K-major, N, M = 128.
+    static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+                                       ((uint32_t)(kLhM >> 4) << 24);
+    static size_t smem() {
+        return 1024 + kLhStages * (size_t)(kLhStageA + kStageB) + 4 * (size_t)kOutTile + sizeof(LhShared);
+    }
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -132,12 +138,12 @@ __device__ __forceinline__ unsigned long long sw128_desc(uint32_t saddr) {
            | (2ull << 61);                                // 128-byte swizzle
 }
 __device__ __forceinline__ void umma_bf16(uint32_t dtmem, unsigned long long adesc, unsigned long long bdesc,
-                                          uint32_t accumulate) {
+                                          uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
-        "l"(adesc), "l"(bdesc), "r"(kLhIdesc), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
@@ -156,10 +162,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+template <int N>
 __global__ void __launch_bounds__(kLhThreads, 1)
 lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int tma_out, __nv_bfloat16* __restrict__ out, int B,
-               int V, int K, int ntiles, int* __restrict__ err) {
+               int V, int K, int ntiles, int* __restrict__ err, const __grid_constant__ LhPeer peer) {
+    using Tl = LhTile<N>;
+    constexpr uint32_t kLhStageB = Tl::kStageB;
+    constexpr uint32_t kLhOutTile = Tl::kOutTile;
+    constexpr int kLhN = N;
     extern __shared__ unsigned char lh_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(lh_raw) + 1023) & ~(uintptr_t)1023);
@@ -243,7 +254,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint32_t b0 = smem_u32(sB + s * kLhStageB);
 #pragma unroll
                     for (int kk = 0; kk < kLhK / 16; kk++)
-                        umma_bf16(dt, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32),
+                        umma_bf16(dt, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), Tl::kIdesc,
                                   (kb | kk) != 0 ? 1u : 0u);
                     umma_commit(&sh->empty[s]);
                     last_bar = &sh->empty[s];
@@ -260,8 +271,13 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // ---- epilogue: warps 2..5, each on its quarter of the TMEM lanes
         // (32 batch rows).  With tma_out the warp stages its rows of the tile
         // in shared memory and one lane stores them with a TMA bulk tensor
-        // copy (whole 416-byte row segments; rows past B and columns past V
-        // are clipped by the copy); otherwise each lane stores its own row.
+        // copy (whole row segments; rows past B and columns past V are
+        // clipped by the copy).  In a sharded launch (peer.nranks > 0) the
+        // warp stages its rows the same way and then writes each row segment
+        // to the buffer of the rank that samples that row (this GPU's or a
+        // peer's over NVLink), 16 bytes per lane.  Otherwise each lane stores
+        // its own row.
+        const bool staged = tma_out || peer.nranks > 0;
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const bool vec = (V % 8) == 0;
@@ -287,7 +303,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                                                   __uint_as_float(r[2 * j + 1]));
                     pk[j] = *reinterpret_cast<const uint32_t*>(&h);
                 }
-                if (tma_out) {
+                if (staged) {
                     uint4* d4 = reinterpret_cast<uint4*>(stage + c * 16);
                     d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
@@ -320,9 +336,25 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
             }
+            // (the accumulator is released above: its values are in the staging rows)
+            if (peer.nranks > 0) {
+                const uint4* rows = reinterpret_cast<const uint4*>(sC + q * kLhOutTile);
+                constexpr int kChunks = kLhN / 8;  // 16-byte pieces of a staged row
+                for (int rr = 0; rr < 32; rr++) {
+                    const int grow = peer.row0 + q * 32 + rr;
+                    if (q * 32 + rr >= B) break;
+                    const int rk = grow / peer.rows_per;
+                    uint4* drow = reinterpret_cast<uint4*>(peer.dst[rk] + (size_t)(grow - rk * peer.rows_per) * peer.ld +
+                                                           peer.col0 + n0);
+                    for (int c = lane; c < kChunks; c += 32)
+                        if (n0 + c * 8 < V) drow[c] = rows[rr * kChunks + c];
+                }
+                __syncwarp();
+            }
         }
         if (tma_out && lane == 0)  // the last stores complete before the CTA leaves
             asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if (peer.nranks > 0) __threadfence_system();  // peer stores visible before the kernel ends
     }
     tc_fence_before();
     __syncthreads();
@@ -393,34 +425,76 @@ static bool make_map(CUtensorMap* m, const void* ptr, int rows, int K, int box_r
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// logits[B, V] = bf16(normed[B, K] . W[V, K]^T); B <= 128, K % 64 == 0.
-// Returns cudaErrorInvalidValue when a tensor map cannot be built.
-cudaError_t launch_lm_head(const __nv_bfloat16* normed, const __nv_bfloat16* W, __nv_bfloat16* logits,
-                           int B, int V, int K, int num_sms, int* err, cudaStream_t stream) {
-    CUtensorMap ma, mb;
-    if (!make_map(&ma, normed, B, K, kLhM) || !make_map(&mb, W, V, K, kLhN)) return cudaErrorInvalidValue;
-    // the logits as [B, V] with 32-row x kLhN-column boxes, unswizzled (row
+template <int N>
+static cudaError_t lm_head_go(const CUtensorMap& ma, const __nv_bfloat16* W, __nv_bfloat16* logits, int B,
+                              int V, int K, int num_sms, int* err, const LhPeer& peer, cudaStream_t stream) {
+    CUtensorMap mb;
+    if (!make_map(&mb, W, V, K, N)) return cudaErrorInvalidValue;
+    // the logits as [B, V] with 32-row x N-column boxes, unswizzled (row
     // pitch V * 2 bytes must be a multiple of 16)
     CUtensorMap mc;
     memset(&mc, 0, sizeof(mc));
     int tma_out = 0;
-    if ((V % 8) == 0 && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0)) {
+    if (peer.nranks == 0 && (V % 8) == 0 && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0)) {
         auto fn = encode_fn();
         const cuuint64_t dims[2] = {(cuuint64_t)V, (cuuint64_t)B};
         const cuuint64_t strides[1] = {(cuuint64_t)V * 2};
-        const cuuint32_t box[2] = {(cuuint32_t)kLhN, 32};
+        const cuuint32_t box[2] = {(cuuint32_t)N, 32};
         const cuuint32_t estr[2] = {1, 1};
         tma_out = fn && fn(&mc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, logits, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
-    const int ntiles = (V + kLhN - 1) / kLhN;
+    const int ntiles = (V + N - 1) / N;
     const int grid = ntiles < num_sms ? ntiles : num_sms;
-    const size_t smem = lm_head_smem();
-    cudaError_t e = cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = LhTile<N>::smem();
+    cudaError_t e = cudaFuncSetAttribute(lm_head_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    lm_head_kernel<<<grid, kLhThreads, smem, stream>>>(ma, mb, mc, tma_out, logits, B, V, K, ntiles, err);
+    lm_head_kernel<N><<<grid, kLhThreads, smem, stream>>>(ma, mb, mc, tma_out, logits, B, V, K, ntiles, err, peer);
     return cudaGetLastError();
+}
+
+// The tile width whose tiles spread most evenly over num_sms persistent CTAs
+// (time ~ waves x N); ties go to the wider tile.
+int lm_head_tile(int V, int num_sms) {
+    static const int cand[] = {208, 176, 144, 128};
+    int best = cand[0];
+    long long best_cost = -1;
+    for (int n : cand) {
+        const long long tiles = (V + n - 1) / n;
+        const long long cost = ((tiles + num_sms - 1) / num_sms) * n;
+        if (best_cost < 0 || cost < best_cost) { best = n; best_cost = cost; }
+    }
+    return best;
+}
+
+static cudaError_t lm_head_dispatch(const __nv_bfloat16* normed, const __nv_bfloat16* W, __nv_bfloat16* logits,
+                                    int B, int V, int K, int num_sms, int* err, const LhPeer& peer,
+                                    cudaStream_t stream) {
+    CUtensorMap ma;
+    if (!make_map(&ma, normed, B, K, kLhM)) return cudaErrorInvalidValue;
+    switch (lm_head_tile(V, num_sms)) {
+        case 176: return lm_head_go<176>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
+        case 144: return lm_head_go<144>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
+        case 128: return lm_head_go<128>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
+        default: return lm_head_go<208>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
+    }
+}
+
+// logits[B, V] = bf16(normed[B, K] . W[V, K]^T); B <= 128, K % 64 == 0.
+// Returns cudaErrorInvalidValue when a tensor map cannot be built.
+cudaError_t launch_lm_head(const __nv_bfloat16* normed, const __nv_bfloat16* W, __nv_bfloat16* logits,
+                           int B, int V, int K, int num_sms, int* err, cudaStream_t stream) {
+    LhPeer none;
+    memset(&none, 0, sizeof(none));
+    return lm_head_dispatch(normed, W, logits, B, V, K, num_sms, err, none, stream);
+}
+
+// One vocabulary slice: logits of W_shard's `cols` rows for B <= 128 batch
+// rows, each stored to the rank that samples it (see LhPeer).
+cudaError_t launch_lm_head_shard(const __nv_bfloat16* normed, const __nv_bfloat16* W_shard, int B, int cols,
+                                 int K, int num_sms, int* err, const LhPeer& peer, cudaStream_t stream) {
+    return lm_head_dispatch(normed, W_shard, nullptr, B, cols, K, num_sms, err, peer, stream);
 }
 
 cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int B, int D,

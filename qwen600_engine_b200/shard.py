@@ -9,9 +9,18 @@ only collective is the gather of the int32 tokens (and, when asked, the RNG
 states) to one rank, plus the max-over-ranks of the timed region.
 
 The functions take a torch.distributed process group (NCCL on GPUs, gloo in
-the CPU tests) and plain tensors; nothing here depends on the sampler
-library.
+the CPU tests) and plain tensors; nothing above ``VocabShardedLmHead``
+depends on the sampler library.
+
+The decode tail (final RMSNorm + lm_head, qwen_model.cuh:710-723) shards the
+other way: splitting its rows would make every GPU stream the whole 311 MB
+weight, so ``VocabShardedLmHead`` splits the vocabulary (``vocab_shard``).
+Each GPU computes its slice of every row's logits and stores each row segment
+straight into the buffer of the GPU that samples that row (peer stores over
+NVLink inside the lm_head kernel); after one completion barrier every GPU
+holds whole rows of its ``row_block`` and samples them as above.
 """
+import ctypes as C
 from typing import List, Optional, Tuple
 
 import numpy as np
@@ -69,3 +78,119 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+def vocab_shard(rank: int, world: int, vocab: int, align: int = 8) -> Tuple[int, int]:
+    """Columns [col0, col0 + cols) of the vocabulary held by ``rank``:
+    contiguous slices of ceil(vocab / world) rounded up to ``align`` columns
+    (the last ones shorter or empty)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank outside [0, world)")
+    per = -(-vocab // world)
+    per = -(-per // align) * align
+    col0 = min(rank * per, vocab)
+    return col0, min(col0 + per, vocab) - col0
+
+
+class VocabShardedLmHead:
+    """The decode tail on ``world`` GPUs, one process each, vocabulary-sharded.
+
+    ``weight_shard`` is this rank's rows [col0, col0 + cols) of the tied
+    lm_head / embedding weight (bf16 [cols, hidden_dim] on this rank's GPU;
+    ``vocab_shard`` gives the split).  Each call takes the same final hidden
+    rows on every rank, computes this rank's slice of every row's logits
+    (``qs_lm_head_shard``) and returns this rank's ``row_block`` of whole
+    logit rows, bit-identical to the single-GPU ``lm_head``.  The row buffers
+    are mapped between the processes once, at construction (CUDA IPC; every
+    rank must construct and ``close`` together, since both exchange over the
+    process group)."""
+
+    def __init__(self, weight_shard, col0: int, vocab: int, max_batch: int, *, rank: int, world: int,
+                 group=None):
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+        from .sampler import _wrap_device
+        if weight_shard.dtype != torch.bfloat16 or weight_shard.dim() != 2 or not weight_shard.is_cuda:
+            raise ValueError("weight_shard must be a bf16 [cols, hidden_dim] CUDA tensor")
+        if world > 8:
+            raise ValueError("at most 8 ranks")
+        self.lib = _lib.lib
+        self.weight = weight_shard.contiguous()
+        self.col0, self.cols = int(col0), int(self.weight.shape[0])
+        self.vocab, self.max_batch = int(vocab), int(max_batch)
+        self.rank, self.world, self.group = rank, world, group
+        self.device = self.weight.device
+        self.hidden_dim = int(self.weight.shape[1])
+        self.rows_cap = -(-self.max_batch // world)
+        nbytes = self.rows_cap * self.vocab * 2
+        hb = self.lib.qs_ipc_handle_bytes()
+        handle = (C.c_ubyte * hb)()
+        own = C.c_void_p()
+        _lib.check(self.lib.qs_ipc_alloc(nbytes, C.byref(own), handle))
+        self._own = own.value
+        self._peers: List[int] = []
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        parts = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine, group=group)
+        ptrs = []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self._own)
+                continue
+            h = (C.c_ubyte * hb).from_buffer_copy(bytes(parts[r].cpu().tolist()))
+            q = C.c_void_p()
+            _lib.check(self.lib.qs_ipc_open(h, C.byref(q)))
+            self._peers.append(q.value)
+            ptrs.append(q.value)
+        self._dst = (C.c_void_p * world)(*ptrs)
+        dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.rows = _wrap_device(self._own, (self.rows_cap, self.vocab), torch.bfloat16, dev)
+        self.normed = torch.empty((self.max_batch, self.hidden_dim), dtype=torch.bfloat16, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def __call__(self, hidden, norm_weight=None, stream=None, weight=None):
+        """This rank's rows [start, stop) of ``row_block(rank, world, B)`` as a
+        bf16 [stop - start, vocab] view of its row buffer (valid until the
+        next call).  ``weight`` replaces the shard for this call (same shape)."""
+        import torch.distributed as dist
+        from . import _lib
+        from .sampler import _ptr, _stream_handle
+        B = int(hidden.shape[0])
+        if B > self.max_batch or int(hidden.shape[1]) != self.hidden_dim:
+            raise ValueError("hidden must be [B <= max_batch, hidden_dim]")
+        per = max(1, -(-B // self.world))
+        w = self.weight if weight is None else weight
+        if tuple(w.shape) != tuple(self.weight.shape) or w.dtype != self.weight.dtype:
+            raise ValueError("weight must have the shard's shape and dtype")
+        _lib.check(self.lib.qs_lm_head_shard(_ptr(hidden), _ptr(norm_weight), _ptr(w), B,
+                                             self.hidden_dim, self.vocab, self.col0, self.cols,
+                                             _ptr(self.normed), self._dst, self.world, per,
+                                             _ptr(self.err), _stream_handle(stream)))
+        # every rank's stores have landed once every rank's kernel is done
+        dist.all_reduce(self._flag, group=self.group)
+        start, stop = row_block(self.rank, self.world, B)
+        return self.rows[:stop - start]
+
+    def status(self) -> None:
+        """Raises if a kernel gave up waiting on its own pipeline."""
+        from . import _lib
+        if int(self.err.item()) != 0:
+            raise _lib.SamplerError(_lib.QS_ERR_CUDA, "lm_head kernel gave up waiting on its pipeline")
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers, then (after every rank has) frees this
+        rank's own."""
+        import torch
+        import torch.distributed as dist
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for p in self._peers:
+            self.lib.qs_ipc_close(C.c_void_p(p))
+        self._peers = []
+        dist.barrier(group=self.group)
+        self.rows = None
+        self.lib.qs_ipc_free(C.c_void_p(self._own))
+        self._own = None

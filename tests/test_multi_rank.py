@@ -80,3 +80,54 @@ def test_two_ranks_gather_equals_one_process(tmp_path, B):
     np.testing.assert_array_equal(got["tokens"], want["tokens"])
     np.testing.assert_array_equal(got["rng"], want["rng"])
     assert float(got["slowest"]) == 2.5
+
+
+def test_vocab_shards_cover_the_vocabulary():
+    for V in (8, 4096, 20008, 151936):
+        for G in (1, 2, 3, 4, 8):
+            sh = [shard.vocab_shard(r, G, V) for r in range(G)]
+            assert sh[0][0] == 0 and sh[-1][0] + sh[-1][1] == V
+            for (c0, n0), (c1, n1) in zip(sh, sh[1:]):
+                assert c0 + n0 == c1 and c1 % 8 == 0 and n0 >= 0
+            assert all(n % 8 == 0 for _, n in sh[:-1])
+
+
+def _vocab_rank_main(rank, world, port, B, V, K, out_path):
+    """Each rank computes its vocabulary slice of every row's logits; the
+    slices are exchanged and each rank keeps whole rows of its row block --
+    the data movement the sharded lm_head kernel does with peer stores."""
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(3)
+        W = torch.randn(V, K, generator=g)
+        h = torch.randn(B, K, generator=g)
+        c0, n = shard.vocab_shard(rank, world, V)
+        part = (h @ W[c0:c0 + n].T).to(torch.bfloat16).float()
+        width = max(shard.vocab_shard(r, world, V)[1] for r in range(world))
+        pad = torch.zeros(B, width)
+        pad[:, :n] = part
+        parts = [torch.empty_like(pad) for _ in range(world)]
+        dist.all_gather(parts, pad)
+        a, b = shard.row_block(rank, world, B)
+        rows = torch.empty(b - a, V)
+        for r in range(world):
+            rc0, rn = shard.vocab_shard(r, world, V)
+            rows[:, rc0:rc0 + rn] = parts[r][a:b, :rn]
+        full = (h @ W.T).to(torch.bfloat16).float()[a:b]
+        np.save(out_path + f".{rank}.npy", np.array([torch.equal(rows, full)]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("B", [6, 7])
+def test_two_ranks_vocab_slices_rebuild_rows(tmp_path, B):
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "v")
+    mp.start_processes(_vocab_rank_main, args=(2, _free_port(), B, 1000, 64, out), nprocs=2,
+                       start_method="spawn")
+    for r in range(2):
+        assert bool(np.load(out + f".{r}.npy")[0])
