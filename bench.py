@@ -344,10 +344,17 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-lm-head", dest="lm_head", action="store_false",
                     help="skip the RMSNorm + lm_head measurement")
+    ap.add_argument("--only-lm-head", action="store_true",
+                    help="one GPU: run only the decode-tail measurement (configuration 5) and print it")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.only_lm_head:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps({"lm_head": measure_lm_head(torch, torch.device("cuda", 0))}), flush=True)
+        return 0
 
     import torch
     import torch.distributed as dist

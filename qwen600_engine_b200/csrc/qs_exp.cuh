@@ -63,6 +63,32 @@ static __device__ __forceinline__ float ref_expf(float x, const ExpFix& fx) {
     return ref_expf_fix(x, m, fx);
 }
 
+// ref_expf of N values at once, for values a thread holds together: the
+// exponentials first, then every filter load, then the rare table searches,
+// so the evaluations overlap instead of each waiting behind a possible call.
+// Bit e of `act` selects x[e]; unselected outputs are 0.  ref_expf_fix repeats
+// the filter's checks, so each output is ref_expf's.
+template <int N>
+__device__ __forceinline__ void ref_expf_batch(const float* x, uint32_t act, float* out, const ExpFix& fx) {
+#pragma unroll
+    for (int e = 0; e < N; e++) out[e] = ((act >> e) & 1u) ? qs_exp_rn(x[e]) : 0.0f;
+    uint32_t need = 0;
+#pragma unroll
+    for (int e = 0; e < N; e++) {
+        const uint32_t u = __float_as_uint(x[e]);
+        const uint32_t a = u & 0x7FFFFFFFu;
+        if (((act >> e) & 1u) && (u & 0x80000000u) && (a >> 16) < fx.nb) {
+            const uint32_t h = exp_fix_hash(a);
+            if ((__ldg(fx.bloom + (h >> 5)) >> (h & 31)) & 1u) need |= 1u << e;
+        }
+    }
+    if (need) {
+#pragma unroll
+        for (int e = 0; e < N; e++)
+            if ((need >> e) & 1u) out[e] = ref_expf_fix(x[e], out[e], fx);
+    }
+}
+
 // One ulp of a finite non-negative float (distance to the next float up).
 __device__ __forceinline__ float ulp_up(float m) {
     return __fsub_rn(__uint_as_float(__float_as_uint(m) + 1u), m);

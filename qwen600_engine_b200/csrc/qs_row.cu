@@ -465,12 +465,15 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
     const int lane = threadIdx.x & 31;
     float v[EPL];
     rv.load(g, lane, v);
-    float ex[EPL];
+    float dd[EPL], ex[EPL];
+    uint32_t act = 0;
 #pragma unroll
     for (int e = 0; e < EPL; e++) {
         const float t = __fmul_rn(v[e], inv);
-        ex[e] = (t >= thr) ? ref_expf(__fsub_rn(t, M), fx) : 0.0f;
+        dd[e] = __fsub_rn(t, M);
+        if (t >= thr) act |= 1u << e;
     }
+    ref_expf_batch<EPL>(dd, act, ex, fx);
 #pragma unroll
     for (int e = 0; e < EPL; e += 4)
         *reinterpret_cast<float4*>(buf + lane * EPL + e) = make_float4(ex[e], ex[e + 1], ex[e + 2], ex[e + 3]);
@@ -690,21 +693,40 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                 // segment to the parity-aware composition.
                 const bool pow2 = (23 - E) >= -126 && (23 - E) <= 127;
                 const float scale = pow2 ? exp2f((float)(23 - E)) : 0.0f;
+                // The fast terms of all EPL elements first (no call in the
+                // loop, so they overlap), then the rare exact terms, then the
+                // increments.
                 uint32_t inc = 0;
                 bool ok = true, tie = false;
+                float xs[EPL];
+                uint32_t act = 0, nearm = 0;
 #pragma unroll
                 for (int e = 0; e < EPL; e++) {
                     const float t = __fmul_rn(v[e], inv);
+                    xs[e] = 0.0f;
                     if (t >= thr) {
-                        const float d = __fsub_rn(t, M);
-                        float term = expf(d);
-                        float x = pow2 ? __fmul_rn(term, scale) : ldexpf(term, 23 - E);
-                        float fr = __fsub_rn(x, floorf(x));
-                        if (!(x < 16777216.0f) || fabsf(__fsub_rn(fr, 0.5f)) <= __fmul_rn(x, 4.8e-7f)) {
-                            term = exact_exp(d, fx);
-                            x = pow2 ? __fmul_rn(term, scale) : ldexpf(term, 23 - E);
-                            fr = __fsub_rn(x, floorf(x));
+                        act |= 1u << e;
+                        const float term = expf(__fsub_rn(t, M));
+                        const float x = pow2 ? __fmul_rn(term, scale) : ldexpf(term, 23 - E);
+                        const float fr = __fsub_rn(x, floorf(x));
+                        if (!(x < 16777216.0f) || fabsf(__fsub_rn(fr, 0.5f)) <= __fmul_rn(x, 4.8e-7f))
+                            nearm |= 1u << e;
+                        xs[e] = x;
+                    }
+                }
+                if (nearm) {
+#pragma unroll
+                    for (int e = 0; e < EPL; e++)
+                        if ((nearm >> e) & 1u) {
+                            const float term = exact_exp(__fsub_rn(__fmul_rn(v[e], inv), M), fx);
+                            xs[e] = pow2 ? __fmul_rn(term, scale) : ldexpf(term, 23 - E);
                         }
+                }
+#pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    if ((act >> e) & 1u) {
+                        const float x = xs[e];
+                        const float fr = __fsub_rn(x, floorf(x));
                         if (!(x < 16777216.0f)) ok = false;
                         else if (fr == 0.5f) tie = true;
                         else inc += (uint32_t)rintf(x);
@@ -1578,7 +1600,20 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     // ---- C: exact softmax denominator (sampler.h:195-201)
     if (!dense) {
         // the stashed terms, then the stash in index order, added in order
-        for (int i = tid; i < nst; i += kRowThreads) st_e[i] = ref_expf(__fsub_rn(st_t[i], M), fx);
+        for (int i0 = tid; i0 < nst; i0 += 4 * kRowThreads) {
+            float x4[4], e4[4];
+            uint32_t act = 0;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * kRowThreads;
+                x4[u] = 0.0f;
+                if (i < nst) { x4[u] = __fsub_rn(st_t[i], M); act |= 1u << u; }
+            }
+            ref_expf_batch<4>(x4, act, e4, fx);
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if ((act >> u) & 1u) st_e[i0 + u * kRowThreads] = e4[u];
+        }
         {
             const int per = (nseg + kRowThreads - 1) / kRowThreads;
             const int c0 = tid * per, c1 = min(c0 + per, nseg);

@@ -155,9 +155,28 @@ sort_kernel(const T* __restrict__ logits, int V, SortParams prm, const int* __re
         RowResult out = res[row];
         const T* L = logits + (size_t)row * V;
         // 1. keys in index order, penalised values substituted
-        for (int i = tid; i < V; i += kSortThreads) {
-            __stcg(kA + i, sort_key(sort_prob(Elem<T>::widen(L[i]), out, fx)));
-            __stcg(iA + i, (uint32_t)i);
+        // (four elements per thread at a time, so their exact exponentials overlap)
+        for (int i0 = tid; i0 < V; i0 += 4 * kSortThreads) {
+            float x4[4], e4[4];
+            uint32_t act = 0;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * kSortThreads;
+                x4[u] = 0.0f;
+                if (i < V) {
+                    x4[u] = __fsub_rn(__fmul_rn(Elem<T>::widen(L[i]), out.inv_temp), out.max_logit);
+                    act |= 1u << u;
+                }
+            }
+            ref_expf_batch<4>(x4, act, e4, fx);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * kSortThreads;
+                if ((act >> u) & 1u) {
+                    __stcg(kA + i, sort_key(__fmul_rn(e4[u], out.sum_inv)));
+                    __stcg(iA + i, (uint32_t)i);
+                }
+            }
         }
         __syncthreads();
         const int nov = ov_n ? ov_n[row] : 0;
