@@ -172,13 +172,14 @@ struct KernelScope {
     }
 };
 
-// Hash filter over the expf correction table (one bit per hashed entry).
+// Blocked hash filter over the expf correction table (two bits of one word
+// per entry; exp_fix_word / exp_fix_bits).
 static const std::vector<uint32_t>& exp_bloom_host() {
     static std::vector<uint32_t> bits = [] {
         std::vector<uint32_t> b((size_t)1 << (kBloomBits - 5), 0u);
         for (size_t i = 0; i < QS_EXP_NENT; i++) {
-            const uint32_t h = exp_fix_hash(qs_exp_fix_ent[i] & 0x7FFFFFFFu);
-            b[h >> 5] |= 1u << (h & 31);
+            const uint32_t a = qs_exp_fix_ent[i] & 0x7FFFFFFFu;
+            b[exp_fix_word(a)] |= exp_fix_bits(a);
         }
         return b;
     }();

@@ -13,14 +13,28 @@ namespace qs {
 struct ExpFix {
     const uint32_t* off;    // [nb + 1] bucket offsets
     const uint32_t* ent;    // |x| bits, bit 31 set when expf = qs_exp_rn + 1 ulp
-    const uint32_t* bloom;  // [1 << (kBloomBits - 5)] words: hash of every entry
+    const uint32_t* bloom;  // [1 << (kBloomBits - 5)] words: two bits of one word per entry
     uint32_t nb;
 };
 
-constexpr int kBloomBits = 24;  // 2 MB filter: ~0.6% false positives for ~97k entries
+constexpr int kBloomBits = 24;  // 2 MB filter
 
-__host__ __device__ __forceinline__ uint32_t exp_fix_hash(uint32_t a) {
-    return (a * 0x9E3779B1u) >> (32 - kBloomBits);
+// Blocked filter: an entry |x| sets four bits (5-bit fields of one hash) of
+// the word chosen by another hash, so a query is one load.  With the ~97k
+// entries in 2^19 words, an input of the sampler's range that is not an entry
+// passes with probability ~0.005% (one bit per entry: ~0.6%); each pass costs
+// a table search of dependent loads.
+__host__ __device__ __forceinline__ uint32_t exp_fix_word(uint32_t a) {
+    return (a * 0x9E3779B1u) >> (32 - (kBloomBits - 5));
+}
+__host__ __device__ __forceinline__ uint32_t exp_fix_bits(uint32_t a) {
+    const uint32_t m = a * 0x85EBCA6Bu;
+    return (1u << (m >> 27)) | (1u << ((m >> 22) & 31u)) | (1u << ((m >> 17) & 31u)) |
+           (1u << ((m >> 12) & 31u));
+}
+__device__ __forceinline__ bool exp_fix_maybe(const ExpFix& fx, uint32_t a) {
+    const uint32_t want = exp_fix_bits(a);
+    return (__ldg(fx.bloom + exp_fix_word(a)) & want) == want;
 }
 
 // qs_exp_rn(x) corrected to the host libm's expf; m = qs_exp_rn(x) precomputed.
@@ -30,8 +44,7 @@ static __device__ __noinline__ float ref_expf_fix(float x, float m, const ExpFix
     a &= 0x7FFFFFFFu;
     const uint32_t b = a >> 16;
     if (b >= fx.nb) return m;
-    const uint32_t h = exp_fix_hash(a);
-    if (!((__ldg(fx.bloom + (h >> 5)) >> (h & 31)) & 1u)) return m;
+    if (!exp_fix_maybe(fx, a)) return m;
     uint32_t lo = __ldg(fx.off + b);
     const uint32_t end = __ldg(fx.off + b + 1);
     uint32_t hi = end;
@@ -58,8 +71,7 @@ static __device__ __forceinline__ float ref_expf(float x, const ExpFix& fx) {
     if (!(a & 0x80000000u)) return m;
     a &= 0x7FFFFFFFu;
     if ((a >> 16) >= fx.nb) return m;
-    const uint32_t h = exp_fix_hash(a);
-    if (!((__ldg(fx.bloom + (h >> 5)) >> (h & 31)) & 1u)) return m;
+    if (!exp_fix_maybe(fx, a)) return m;
     return ref_expf_fix(x, m, fx);
 }
 
@@ -78,8 +90,7 @@ __device__ __forceinline__ void ref_expf_batch(const float* x, uint32_t act, flo
         const uint32_t u = __float_as_uint(x[e]);
         const uint32_t a = u & 0x7FFFFFFFu;
         if (((act >> e) & 1u) && (u & 0x80000000u) && (a >> 16) < fx.nb) {
-            const uint32_t h = exp_fix_hash(a);
-            if ((__ldg(fx.bloom + (h >> 5)) >> (h & 31)) & 1u) need |= 1u << e;
+            if (exp_fix_maybe(fx, a)) need |= 1u << e;
         }
     }
     if (need) {
