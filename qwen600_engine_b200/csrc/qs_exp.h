@@ -51,7 +51,14 @@ QS_HD float qs_exp_rn(float xf) {
     p = fma(p, r, 0x1.0000000000000p-1);         /* 1/2!  */
     p = fma(p, r, 1.0);
     p = fma(p, r, 1.0);
+#ifdef __CUDA_ARCH__
+    /* k is in [-217, 129] here and p in (0.7, 1.5), so p * 2^k is a normal
+     * double and the product by the power of two built from its bits is
+     * exact: the same value ldexp returns, without its general-case code. */
+    return (float)(p * __longlong_as_double((long long)((int)k + 1023) << 52));
+#else
     return (float)ldexp(p, (int)k);
+#endif
 }
 
 #endif
