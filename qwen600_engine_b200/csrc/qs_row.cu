@@ -698,6 +698,10 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                 // increments.
                 uint32_t inc = 0;
                 bool ok = true, tie = false;
+                // x - rint(x) is exact, so its magnitude is the distance to
+                // the nearest grid point: 0.5 marks an exact half-unit, and
+                // 0.5 - that distance is the distance to the half-unit that
+                // the near test compares with the error band.
                 float xs[EPL];
                 uint32_t act = 0, nearm = 0;
 #pragma unroll
@@ -708,8 +712,8 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                         act |= 1u << e;
                         const float term = expf(__fsub_rn(t, M));
                         const float x = pow2 ? __fmul_rn(term, scale) : ldexpf(term, 23 - E);
-                        const float fr = __fsub_rn(x, floorf(x));
-                        if (!(x < 16777216.0f) || fabsf(__fsub_rn(fr, 0.5f)) <= __fmul_rn(x, 4.8e-7f))
+                        const float dist = fabsf(__fsub_rn(x, rintf(x)));
+                        if (!(x < 16777216.0f) || __fsub_rn(0.5f, dist) <= __fmul_rn(x, 4.8e-7f))
                             nearm |= 1u << e;
                         xs[e] = x;
                     }
@@ -726,10 +730,10 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                 for (int e = 0; e < EPL; e++) {
                     if ((act >> e) & 1u) {
                         const float x = xs[e];
-                        const float fr = __fsub_rn(x, floorf(x));
+                        const float q = rintf(x);
                         if (!(x < 16777216.0f)) ok = false;
-                        else if (fr == 0.5f) tie = true;
-                        else inc += (uint32_t)rintf(x);
+                        else if (fabsf(__fsub_rn(x, q)) == 0.5f) tie = true;
+                        else inc += (uint32_t)q;
                     }
                 }
                 if (inc > (1u << 25)) ok = false;
