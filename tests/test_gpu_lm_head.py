@@ -73,7 +73,11 @@ def _check_logits(torch, normed, w, logits):
     assert (d2 <= 2.02 * ulp + 2 * acc).all()
 
 
-@pytest.mark.parametrize("B,D,V", [(128, 1024, W.VOCAB), (5, 64, 1003), (130, 1024, 4096), (1, 1024, 151936)])
+# The launch picks its tile width from the vocabulary size (208 for the whole
+# Qwen3 vocabulary on 148 SMs, 176 for half of it, 144 for a quarter, 128 for
+# small vocabularies): the cases cover every width.
+@pytest.mark.parametrize("B,D,V", [(128, 1024, W.VOCAB), (5, 64, 1003), (130, 1024, 4096), (1, 1024, 151936),
+                                   (96, 1024, 75968), (128, 1024, 37984), (7, 1024, 18992)])
 def test_rmsnorm_and_logits(B, D, V):
     torch = _torch()
     from qwen600_engine_b200.sampler import lm_head
