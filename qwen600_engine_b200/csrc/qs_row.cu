@@ -488,7 +488,7 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
 struct RowSmem {
     size_t segm, segk, segov, ovi, ovv, ofirst, pairs, pcnt, pubr, hotl, region, ct, ci, cp, so, ck,
         rhist, total;
-    size_t segf, rawv, plv, stream_total;  // streaming pass only (overlays the finishing pass's region)
+    size_t rawv, rech, stream_total;  // streaming pass only (overlays the finishing pass's region)
     int nseg, nrounds, scap, ccap, npairs;
     __host__ __device__ static size_t r16(size_t b) { return (b + 15) & ~(size_t)15; }
     __host__ __device__ RowSmem(int V, int seg, int ov_stride, int ccap_, int scap_) {
@@ -522,9 +522,8 @@ struct RowSmem {
         rhist = p; p += r16(4 * 256);
         total = p;
         p = region;
-        segf = p; p += r16(4 * (size_t)nseg);
         rawv = p; p += r16(4 * ovs);
-        plv = p; p += r16(4 * ovs);
+        rech = p; p += r16(4 * ovs);
         stream_total = p;
     }
 };
@@ -1111,9 +1110,8 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     unsigned long long* pairs = (unsigned long long*)(smem + L.pairs);
     float* pcnt = (float*)(smem + L.pcnt);
     uint32_t* pubr = (uint32_t*)(smem + L.pubr);      // per streaming round: max key seen
-    int* segf = (int*)(smem + L.segf);                // first window token of a marked segment
-    float* rawv = (float*)(smem + L.rawv);            // window tokens' raw logits, as streamed
-    float* plv = (float*)(smem + L.plv);              // max of the other elements of the token's lane
+    float* rawv = (float*)(smem + L.rawv);            // window tokens' raw logits
+    int* rech = (int*)(smem + L.rech);                // segments whose maximum is recomputed
     __shared__ RowShared sh;
 
     long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
@@ -1131,9 +1129,7 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     rv.ovi = ovi;
     rv.ovv = ovv;
     rv.nov = 0;
-    // the streaming pass keeps one round of vectors in flight per warp; the
-    // first round is requested before the window is read, so its loads
-    // overlap the construction of the penalty tables
+    // the streaming pass keeps one round of vectors in flight per warp
     uint4 r[U];
     auto request = [&](int jj) {
         const int gb = jj * kRowRound + warp;
@@ -1145,13 +1141,53 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         }
     };
     request(0);
+    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); sh.misc[6] = 0; sh.misc[7] = 0; }
+    for (int g = tid; g < nseg; g += kRowThreads) segov[g] = 0;
+    stamp(1);
+
+    // ---- A: streaming pass: the maximum of each segment of the raw logits
+    // (the penalty window is applied after the pass).  r holds this round's
+    // vectors; the next round's are requested as soon as this round's maxima
+    // are taken.
+    for (int j = 0; j < L.nrounds; j++) {
+        const int g0 = j * kRowRound + warp;
+        unsigned slow = 0;  // partial segments (warp-uniform)
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int g = g0 + u * kRowWarps;
+            if (g < nseg) {
+                if (rv.aligned && (g + 1) * SEG <= V) {
+                    const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(vec_max<T>(r[u])));
+                    if (lane == 0) segm[g] = fkey_inv(km);
+                } else {
+                    slow |= 1u << u;
+                }
+            }
+        }
+        while (slow) {
+            const int u = __ffs(slow) - 1;
+            slow &= slow - 1;
+            const int g = g0 + u * kRowWarps;
+            // the segment's vector is still in r[u]; partial lanes read -inf
+            // past the row
+            uint4 ru = r[0];
+#pragma unroll
+            for (int q = 1; q < U; q++)
+                if (q == u) ru = r[q];
+            float v[EPL];
+            rv.widen_raw(g, lane, rv.full(g, lane), ru, v);
+            float m = v[0];
+#pragma unroll
+            for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
+            const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
+            if (lane == 0) segm[g] = fkey_inv(km);
+        }
+        if (j + 1 < L.nrounds) request(j + 1);  // r is free: every maximum of this round is taken
+    }
+    __syncthreads();
 
     // ---- the row's penalty window (sampler.h:114-141): slots sorted by
-    // (token, slot), distinct tokens and the slot range of each; the values
-    // are formed from the raw logits as the streaming pass reads them
-    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); sh.misc[7] = 0; }
-    for (int g = tid; g < nseg; g += kRowThreads) segov[g] = 0;
-    for (int j = tid; j < L.nrounds; j += kRowThreads) pubr[j] = fkey(-INFINITY);
+    // (token, slot), distinct tokens and the slot range of each
     int cntw = (win.hist && win.count) ? win.count[row] : 0;
     cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
     const bool pen_on = cntw > 0 && (win.rp != 1.0f || win.fp != 0.0f || win.pp != 0.0f);
@@ -1212,96 +1248,15 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         }
         nov = tot;
         __syncthreads();
-        // mark the segments holding window tokens; the penalised values are
-        // formed after the streaming pass from the raw logits it captures
-        for (int j = tid; j < nov; j += kRowThreads) {
-            const int g = ovi[j] / SEG;
-            segov[g] = 1;
-            if (j == 0 || ovi[j - 1] / SEG != g) segf[g] = j;
-        }
-    }
-    if (tid == 0 && win.ov_n) win.ov_n[row] = nov;
-    __syncthreads();
-
-    rv.nov = nov;
-    stamp(1);
-
-    // ---- A: streaming pass: the maximum of each segment of the penalised
-    // logits.  r holds this round's vectors; the next round's are requested
-    // as soon as this round's maxima are taken.
-    for (int j = 0; j < L.nrounds; j++) {
-        const int g0 = j * kRowRound + warp;
-        unsigned slow = 0;  // segments that are partial or hold overrides (warp-uniform)
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int g = g0 + u * kRowWarps;
-            if (g < nseg) {
-                if (rv.aligned && (g + 1) * SEG <= V && !segov[g]) {
-                    const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(vec_max<T>(r[u])));
-                    if (lane == 0) segm[g] = fkey_inv(km);
-                } else {
-                    slow |= 1u << u;
-                }
-            }
-        }
-        while (slow) {
-            const int u = __ffs(slow) - 1;
-            slow &= slow - 1;
-            const int g = g0 + u * kRowWarps;
-            // the segment's vector is still in r[u]; partial lanes read -inf
-            // past the row
-            uint4 ru = r[0];
-#pragma unroll
-            for (int q = 1; q < U; q++)
-                if (q == u) ru = r[q];
-            float v[EPL];
-            rv.widen_raw(g, lane, rv.full(g, lane), ru, v);
-            // Window tokens are left out here.  A lane holding one records the
-            // token's raw logit and the fmaxf of its other elements (from a NaN
-            // start, fmaxf's identity), and offers the smallest order key; the
-            // fold after the penalties are replayed completes its maximum.
-            const int base = g * SEG + lane * EPL;
-            uint32_t own = 0;
-            int k0 = 0, k1 = 0;
-            if (segov[g]) {
-                k0 = segf[g];
-                k1 = k0;
-                while (k1 < nov && ovi[k1] < (g + 1) * SEG) {
-                    const int p = ovi[k1] - base;
-                    if (p >= 0 && p < EPL) own |= 1u << p;
-                    k1++;
-                }
-            }
-            float m = __uint_as_float(0x7fffffffu);
-#pragma unroll
-            for (int e = 0; e < EPL; e++)
-                if (!((own >> e) & 1u)) m = fmaxf(m, v[e]);
-            if (own) {
-                for (int k = k0; k < k1; k++) {
-                    const int p = ovi[k] - base;
-                    if (p >= 0 && p < EPL) {
-                        float x = v[0];
-#pragma unroll
-                        for (int e = 1; e < EPL; e++)
-                            if (e == p) x = v[e];
-                        rawv[k] = x;
-                        plv[k] = m;
-                    }
-                }
-            }
-            const uint32_t km = __reduce_max_sync(0xffffffffu, own ? 0u : fkey(m));
-            if (lane == 0) segm[g] = fkey_inv(km);
-        }
-        if (j + 1 < L.nrounds) request(j + 1);  // r is free: every maximum of this round is taken
-    }
-    __syncthreads();
-    if (nov > 0) {
-        // each window token's penalised value from the raw logit the pass
-        // captured, replaying its occurrences in slot order (sampler.h:114-141)
         const int nv = sh.misc[7];
+        // each window token's penalised value from its raw logit, replaying
+        // its occurrences in slot order
+        const T* Lrow = logits + (size_t)row * V;
         for (int j = tid; j < nov; j += kRowThreads) {
+            const int t = ovi[j];
             const int q1 = (j + 1 < nov) ? ofirst[j + 1] : nv;
-            float x = rawv[j];
+            const float raw = Elem<T>::widen(Lrow[t]);
+            float x = raw;
             for (int q = ofirst[j]; q < q1; q++) {
                 if (win.rp != 1.0f) x = (x > 0.0f) ? __fdiv_rn(x, win.rp) : __fmul_rn(x, win.rp);
                 if (win.fp != 0.0f)
@@ -1309,33 +1264,50 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
                 if (win.pp != 0.0f) x = __fsub_rn(x, win.pp);
             }
             ovv[j] = x;
+            rawv[j] = raw;
+            segov[t / SEG] = 1;
             if (win.ov_idx) {
-                win.ov_idx[(size_t)row * win.ov_stride + j] = ovi[j];
+                win.ov_idx[(size_t)row * win.ov_stride + j] = t;
                 win.ov_val[(size_t)row * win.ov_stride + j] = x;
             }
         }
         __syncthreads();
-        // fold: per marked segment, each lane that held window tokens offers
-        // the fmaxf of its other elements and its penalised tokens, compared
-        // by order key with the rest of the segment as the warp reduction does
+        // Fold, per segment holding window tokens (its first token's thread).
+        // When no token's raw logit equals the segment's raw maximum, the
+        // other elements hold that maximum, so the maximum of the penalised
+        // segment is the fmaxf of it and the penalised tokens.  Otherwise, or
+        // where a NaN or a zero is involved (fmaxf and the order keys may
+        // pick differently there), the segment is recomputed below with the
+        // penalised values substituted, as the streaming pass would have.
         for (int j = tid; j < nov; j += kRowThreads) {
             const int g = ovi[j] / SEG;
-            if (segf[g] != j) continue;
-            uint32_t km = fkey(segm[g]);
-            int k = j;
-            while (k < nov && ovi[k] / SEG == g) {
-                const int lk = (ovi[k] - g * SEG) / EPL;
-                float q = plv[k];
-                while (k < nov && ovi[k] / SEG == g && (ovi[k] - g * SEG) / EPL == lk) {
-                    q = fmaxf(q, ovv[k]);
-                    k++;
-                }
-                km = max(km, fkey(q));
+            if (j > 0 && ovi[j - 1] / SEG == g) continue;
+            const float sraw = segm[g];
+            float m = sraw;
+            bool redo = !(sraw == sraw) || sraw == 0.0f;
+            for (int k = j; k < nov && ovi[k] / SEG == g; k++) {
+                const float pv = ovv[k];
+                redo = redo || rawv[k] == sraw || !(pv == pv) || pv == 0.0f;
+                m = fmaxf(m, pv);
             }
-            segm[g] = fkey_inv(km);
+            if (redo) rech[atomicAdd(&sh.misc[6], 1)] = g;
+            else segm[g] = m;
         }
         __syncthreads();
     }
+    if (tid == 0 && win.ov_n) win.ov_n[row] = nov;
+    rv.nov = nov;
+    for (int i = warp; i < sh.misc[6]; i += kRowWarps) {
+        const int g = rech[i];
+        float v[EPL];
+        rv.load(g, lane, v);
+        float m = v[0];
+#pragma unroll
+        for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
+        const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
+        if (lane == 0) segm[g] = fkey_inv(km);
+    }
+    __syncthreads();
     float lm = -INFINITY;
     for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
     const float maxl = rblock_max(lm, sh.red_f);
