@@ -484,6 +484,15 @@ __device__ __noinline__ float walk_segment(const RowView<T>& rv, int g, float th
     return s;
 }
 
+// 4-byte asynchronous copy global -> shared (completes at cp_async_wait_all).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Shared-memory layout of one row, shared by the kernel and its launcher.
 struct RowSmem {
     size_t segm, segk, segov, ovi, ovv, ofirst, pairs, pcnt, pubr, hotl, region, ct, ci, cp, so, ck,
@@ -1143,6 +1152,18 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     request(0);
     if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); sh.misc[6] = 0; sh.misc[7] = 0; }
     for (int g = tid; g < nseg; g += kRowThreads) segov[g] = 0;
+    // the window's slots, their counts and the row's slot count travel to
+    // shared memory while the row streams (asynchronous copies hold no
+    // registers); the slots are staged in ofirst, rebuilt from them later
+    const bool pen_possible = win.hist && win.count && (win.rp != 1.0f || win.fp != 0.0f || win.pp != 0.0f);
+    if (pen_possible) {
+        for (int i = tid; i < win.window; i += kRowThreads) {
+            cp_async4(ofirst + i, win.hist + (size_t)row * win.window + i);
+            if (win.slot_counts) cp_async4(pcnt + i, win.slot_counts + (size_t)row * win.window + i);
+        }
+        if (tid == 0) cp_async4(&sh.misc[5], win.count + row);
+        cp_async_commit();
+    }
     stamp(1);
 
     // ---- A: streaming pass: the maximum of each segment of the raw logits
@@ -1184,22 +1205,33 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         }
         if (j + 1 < L.nrounds) request(j + 1);  // r is free: every maximum of this round is taken
     }
+    if (pen_possible) cp_async_wait_all();
     __syncthreads();
 
     // ---- the row's penalty window (sampler.h:114-141): slots sorted by
     // (token, slot), distinct tokens and the slot range of each
-    int cntw = (win.hist && win.count) ? win.count[row] : 0;
+    int cntw = pen_possible ? sh.misc[5] : 0;
     cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
-    const bool pen_on = cntw > 0 && (win.rp != 1.0f || win.fp != 0.0f || win.pp != 0.0f);
+    const bool pen_on = cntw > 0;
     int nov = 0;
     if (pen_on) {
         int npow = 1;
         while (npow < cntw) npow <<= 1;
         unsigned long long* keys = pairs + npow;  // unsorted (token, slot) keys
+        float* rawslot = reinterpret_cast<float*>(rech);  // raw logit of each slot's token
+        const T* Lrow = logits + (size_t)row * V;
+        float raw0 = 0.0f;  // this thread's first slot: its load overlaps the sort
+        bool has0 = false;
         for (int i = tid; i < npow; i += kRowThreads) {
-            const int t = i < cntw ? win.hist[(size_t)row * win.window + i] : -1;
-            keys[i] = (t >= 0 && t < V) ? (((unsigned long long)(unsigned)t << 32) | (unsigned)i) : ~0ull;
-            if (i < cntw) pcnt[i] = win.slot_counts ? win.slot_counts[(size_t)row * win.window + i] : 0.0f;
+            const int t = i < cntw ? ofirst[i] : -1;
+            const bool valid = t >= 0 && t < V;
+            keys[i] = valid ? (((unsigned long long)(unsigned)t << 32) | (unsigned)i) : ~0ull;
+            if (i < cntw && !win.slot_counts) pcnt[i] = 0.0f;
+            if (valid) {
+                const float raw = Elem<T>::widen(Lrow[t]);
+                if (i == tid) { raw0 = raw; has0 = true; }
+                else rawslot[i] = raw;
+            }
         }
         __syncthreads();
         if (npow <= 256) {
@@ -1227,6 +1259,7 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
                 }
             }
         }
+        if (has0) rawslot[tid] = raw0;
         // distinct tokens: rank by an exclusive scan of "first of its token" flags
         const int per = (npow + kRowThreads - 1) / kRowThreads;
         const int c0 = tid * per, c1 = min(c0 + per, npow);
@@ -1249,13 +1282,12 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         nov = tot;
         __syncthreads();
         const int nv = sh.misc[7];
-        // each window token's penalised value from its raw logit, replaying
-        // its occurrences in slot order
-        const T* Lrow = logits + (size_t)row * V;
+        // each window token's penalised value from its raw logit (that of its
+        // first slot), replaying its occurrences in slot order
         for (int j = tid; j < nov; j += kRowThreads) {
             const int t = ovi[j];
             const int q1 = (j + 1 < nov) ? ofirst[j + 1] : nv;
-            const float raw = Elem<T>::widen(Lrow[t]);
+            const float raw = rawslot[(int)(pairs[ofirst[j]] & 0xFFFFFFFFull)];
             float x = raw;
             for (int q = ofirst[j]; q < q1; q++) {
                 if (win.rp != 1.0f) x = (x > 0.0f) ? __fdiv_rn(x, win.rp) : __fmul_rn(x, win.rp);
