@@ -302,6 +302,19 @@ __device__ __forceinline__ void do_swaps(const Arr& A, const Pos& posL, const Po
     }
 }
 
+// Drops whole 128-byte L2 lines of part `part` (of `nparts` equal byte
+// shares) of [p, p + n) without writing them back (their contents become
+// undefined): for scratch that is dead, so that its dirty lines cost no DRAM
+// bandwidth when they would be evicted.  Lines that straddle a share's ends
+// are left alone.  Every thread of the CTA takes a share of the part.
+__device__ __forceinline__ void discard_l2_part(const void* p, size_t n, int part, int nparts) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t a0 = (b + n * (size_t)part / (size_t)nparts + 127) & ~(uintptr_t)127;
+    const uintptr_t a1 = (b + n * (size_t)(part + 1) / (size_t)nparts) & ~(uintptr_t)127;
+    for (uintptr_t a = a0 + (uintptr_t)threadIdx.x * 128; a < a1; a += (uintptr_t)blockDim.x * 128)
+        asm volatile("discard.global.L2 [%0], 128;" ::"l"(a) : "memory");
+}
+
 // The reference's probability of a scaled logit t (sampler.h:197-206).
 __device__ __forceinline__ float prob_of(float t, const RowResult& rr, const ExpFix& fx) {
     return __fmul_rn(ref_expf(__fsub_rn(t, rr.max_logit), fx), rr.sum_inv);
@@ -603,6 +616,18 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
         // the others leave now (none of them touches a peer's shared memory
         // again, and no cluster barrier follows), freeing their SMs
         const bool more = li + ncl < nslow;
+        if (!more && lo >= 0 && lo <= hi && hi < V) {
+            // After the cluster's last row only the first CTA reads the
+            // scratch again, and only keys [lo, hi] and indices [0, max(k, hi + 1)):
+            // every CTA drops its share of the rest from L2 (the position
+            // arrays entirely) while the first continues.
+            const int idx_keep = max(k, hi + 1);
+            discard_l2_part(A.k, sizeof(uint32_t) * (size_t)lo, crank, kTieCluster);
+            discard_l2_part(A.k + hi + 1, sizeof(uint32_t) * (size_t)(V - 1 - hi), crank, kTieCluster);
+            if (idx_keep < V)
+                discard_l2_part(A.idx + idx_keep, sizeof(int) * (size_t)(V - idx_keep), crank, kTieCluster);
+            discard_l2_part(gposL.p, sizeof(int) * 2 * (size_t)V, crank, kTieCluster);
+        }
         if (!more && crank != 0) return;
 
         if (crank == 0) {
