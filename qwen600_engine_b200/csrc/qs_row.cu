@@ -1393,9 +1393,9 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
                   ExpFix fx, int ccap, int scap, RowScratch scr, long long* __restrict__ phase_cycles) {
     constexpr int EPL = Elem<T>::kPerLane;
     constexpr int SEG = 32 * EPL;
-    // gathered segments in flight per warp: 4 (8 held more registers than the
-    // 80 this pass is sized for, and the gather ran ~20% slower)
-    constexpr int U = 4;
+    // gathered segments in flight per warp: 2 (more held more registers than
+    // the 80 this pass is sized for: at 8 the pass ran ~14% slower, at 4 ~4%)
+    constexpr int U = 2;
     const int row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const RowSmem L(V, SEG, win.window, ccap, scap);
