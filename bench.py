@@ -121,86 +121,107 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_reference_sample(target_s: float = 15.0, seed: int = 4):
-    """Times the reference's own sampler.h (oracle/_ref) on this host's cores
-    over a bounded sample of the workload; falls back to the oracle port."""
-    import numpy as np
+def cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    from qwen600_engine_b200 import workloads as W
+
+def reference_runner():
+    """The reference's own sampler.h (oracle/_ref) over all host threads, or
+    the oracle port on one thread where that build is absent.  Returns
+    (run(params, x_f32, hist, counts, count, pos, rng) -> tokens, kind,
+    threads)."""
     threads = os.cpu_count() or 1
-    kind = "reference"
     try:
         from oracle.oracle import RefSampler
         ref = RefSampler()
-        run = lambda wl, x: ref.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
-                                            wl.hist_count, wl.hist_pos, wl.rng, n_threads=threads)
+
+        def run(params, x, hist, counts, count, pos, rng):
+            return ref.sample_rows(params, x, hist, counts, count, pos, rng.copy(),
+                                   n_threads=threads)["tokens"]
+        return run, "reference", threads
     except Exception:
         from oracle.oracle import Oracle
-        kind, threads = "port", 1
         o = Oracle()
-        run = lambda wl, x: o.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
-                                          wl.hist_count, wl.rng)
-    # the reference samples fp32 rows on the host (bf16 widened on the GPU
-    # before its copy-out), so widening happens outside the timed calls
-    probe = W.topk_bf16(B=min(64, 8 * threads), seed=seed)
-    px = probe.logits_f32()
+
+        def run(params, x, hist, counts, count, pos, rng):
+            return o.sample_rows(params, x, hist, counts, count, rng.copy())["tokens"]
+        return run, "port", 1
+
+
+def cpu_leg(params, x, hist, counts, count, rng, gpu_tokens=None, target_s: float = 10.0):
+    """The CPU baseline on a bounded sample: the reference sampler on the same
+    rows the GPU sampled (fp32 logits as the reference reads them, the same
+    windows and initial RNG states), repeated until about `target_s` of wall
+    time; its tokens are also compared with the GPU's (parity of the bench's
+    own rows)."""
+    import numpy as np
+    run, kind, threads = reference_runner()
+    B = x.shape[0]
+    pos = np.zeros(B, np.int32)
     t0 = time.perf_counter()
-    run(probe, px)
+    toks = run(params, x, hist, counts, count, pos, rng)
     dt = time.perf_counter() - t0
-    per_row = dt / probe.batch
-    rows = int(max(probe.batch, min(2048, target_s / max(per_row, 1e-6))))
-    wl = W.topk_bf16(B=rows, seed=seed + 100)
-    wx = wl.logits_f32()
-    # the same rows again until about target_s of CPU time (threads x wall) is spent
-    reps = max(1, min(16, int(target_s / max(per_row * rows * threads, 1e-6))))
+    reps = max(1, min(64, int(target_s / max(dt, 1e-6))))
     t0 = time.perf_counter()
     for _ in range(reps):
-        run(wl, wx)
+        run(params, x, hist, counts, count, pos, rng)
     dt = time.perf_counter() - t0
-    return {"value": reps * rows / dt, "unit": "rows/s", "cores": threads, "kind": kind,
-            "sample": f"{rows} rows of the benchmark workload (seed {seed + 100}) x {reps}, "
-                      f"{dt:.1f} s on {threads} host threads",
-            "seconds": dt, "rows": reps * rows}
+    out = {"value": reps * B / dt, "unit": "rows/s", "cores": threads, "kind": kind,
+           "cpu_model": cpu_model(),
+           "sample": f"the same {B} rows the GPU sampled x {reps} passes, {dt:.1f} s on {threads} host threads"}
+    if gpu_tokens is not None:
+        gt = np.asarray(gpu_tokens)
+        out["parity"] = {"rows": int(B), "tokens_equal": int((gt == toks).sum()),
+                         "checker": kind}
+    return out
 
 
 def run_reference_arm(args):
+    """The reference's own CPU sampler as the job: every step samples the whole
+    batch of the benchmark configuration (1024 rows per GPU of the run) on all
+    host threads.  Rank 0 alone runs; other ranks exit."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import numpy as np
 
     from qwen600_engine_b200 import workloads as W
-    threads = os.cpu_count() or 1
-    try:
-        from oracle.oracle import RefSampler
-        ref = RefSampler()
-        kind = "reference"
-        run = lambda wl, x: ref.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
-                                            wl.hist_count, wl.hist_pos, wl.rng, n_threads=threads)
-    except Exception:
-        from oracle.oracle import Oracle
-        o = Oracle()
-        kind, threads = "port", 1
-        run = lambda wl, x: o.sample_rows(wl.params, x, wl.hist, wl.hist_counts,  # noqa: E731
-                                          wl.hist_count, wl.rng)
-    rows = max(threads * 2, 32)
-    batches = [W.topk_bf16(B=rows, seed=4 + 1000 * i) for i in range(2)]
-    xs = [b.logits_f32() for b in batches]   # widened outside the timing (see cpu_reference_sample)
+    run, kind, threads = reference_runner()
+    rows = args.batch * max(args.gpus, 1)
+    import torch
+    # the benchmark workload drawn on the host (make_inputs' recipe on the CPU
+    # generator), widened to fp32 outside the timing: the reference reads fp32
+    logits, hist, counts, count, rng = make_inputs(torch, rows, 4, torch.device("cpu"))
+    x = logits.float().numpy()
+    h, c, n = hist.numpy(), counts.numpy(), count.numpy()
+    pos = np.zeros(rows, np.int32)
+    st = rng.numpy().view(np.uint64)
+    params = W.SamplingParams(**PARAMS)
+
+    def one(i):
+        run(params, x, h, c, n, pos, st)
     for i in range(args.warmup):
-        run(batches[i % 2], xs[i % 2])
+        one(i)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        run(batches[i % 2], xs[i % 2])
+        one(i)
     dt = time.perf_counter() - t0
     v = rows * args.steps / dt
     line = {"metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "global_batch": rows, "vocab": V,
-                       "rows_per_step": rows, "note": "each step a bounded CPU sample"},
+            "config": {"workload": WORKLOAD, "global_batch": rows, "rows_per_gpu": args.batch,
+                       "vocab": V, "window": WINDOW},
             "cpu_baseline": {"value": v, "unit": "rows/s", "cores": threads, "kind": kind,
-                             "sample": f"{rows} rows per step x {args.steps} steps"},
+                             "cpu_model": cpu_model(),
+                             "sample": f"the whole batch of {rows} rows per step x {args.steps} steps"},
             "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -319,6 +340,157 @@ def measure_lm_head_sharded(torch, dev, rank, world, B=128, K=1024, iters=20):
                     "(one-element NCCL all-reduce)"}
 
 
+def _wl_to_dev(torch, wl, dev):
+    """A workload's logits, window and RNG states as device tensors."""
+    import numpy as np
+    if wl.dtype == "bf16":
+        x = torch.from_numpy(wl.logits.view(np.int16)).to(dev).view(torch.bfloat16)
+    else:
+        x = torch.from_numpy(np.ascontiguousarray(wl.logits)).to(dev)
+    d = {"x": x, "rng": torch.from_numpy(wl.rng.view(np.int64).copy()).to(dev)}
+    if wl.window > 0:
+        d["hist"] = torch.from_numpy(wl.hist.astype(np.int32)).to(dev)
+        d["counts"] = torch.from_numpy(wl.hist_counts.astype(np.float32)).to(dev)
+        d["count"] = torch.from_numpy(wl.hist_count.astype(np.int32)).to(dev)
+    else:
+        d["hist"] = d["counts"] = d["count"] = None
+    return d
+
+
+def _stack(wls):
+    """One workload holding the rows of several (same parameters)."""
+    import numpy as np
+    from qwen600_engine_b200 import workloads as W
+    w0 = wls[0]
+    return W.Workload(w0.name, w0.params, np.concatenate([w.logits for w in wls]), w0.dtype,
+                      np.concatenate([w.hist for w in wls]), np.concatenate([w.hist_counts for w in wls]),
+                      np.concatenate([w.hist_count for w in wls]), np.concatenate([w.hist_pos for w in wls]),
+                      np.concatenate([w.rng for w in wls]), w0.window)
+
+
+def _sampler_for(wl, B, dev):
+    from qwen600_engine_b200.sampler import Sampler
+    p = wl.params
+    return Sampler(p.temperature, p.topp, p.minp, p.top_k, p.repetition_penalty,
+                   p.frequency_penalty, p.presence_penalty, wl.window, 1, max_batch=B,
+                   vocab=wl.vocab, device=dev.index or 0)
+
+
+def _kernel_split(s, run_pass, steps):
+    """Per-kernel CUDA-event times of `steps` more steps (a separate pass)."""
+    import torch
+    s.profile(True)
+    s.profile_reset()
+    run_pass()
+    torch.cuda.synchronize()
+    pr = s.profile_read()
+    s.profile(False)
+    return {k: pr[k] / steps for k in ("stream_ms", "finish_ms", "ties_ms", "emit_ms")}
+
+
+def measure_configs(torch, dev, steps: int, warmup: int, cpu: bool = True):
+    """The other configurations of the headline metric, each on one GPU with
+    its own synthetic inputs (qwen600_engine_b200.workloads), timed with CUDA
+    events on the launching stream over distinct input buffers whose total
+    exceeds L2, and checked against the reference sampler on the same rows:
+
+      1  batch 1, fp32 N(0, 2.5^2) + 8 spikes at +12, 64-token window, k 20:
+         latency of one sampling call (256 distinct rows, each sampled once
+         in the timed pass; its tokens are the parity tokens)
+      2  batch 256, bf16 N(0, 3^2) with duplicate maxima, greedy
+      3  batch 64, fp32 2*Student-t(3), 128-token Zipf window with frequency
+         and presence penalties, top-k off, top-p 0.9 (full-vocabulary nucleus)
+    """
+    import numpy as np
+    from qwen600_engine_b200 import workloads as W
+    hbm, peak_kind = peaks()
+    st = torch.cuda.current_stream()
+    out = {}
+
+    def ev_time(fn, n):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for i in range(n):
+            fn(i)
+        b.record(st)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    def roofline(B, row_bytes, ms, bound):
+        ach = B * row_bytes / (ms * 1e-3) / 1e9
+        return {"bound": bound, "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                "algorithmic_bytes_per_step": B * row_bytes, "peak_source": peak_kind}
+
+    # ---- configuration 1: one row per call
+    rows = _stack([W.single_row(seed=s_) for s_ in range(1, 257)])
+    d = _wl_to_dev(torch, rows, dev)
+    s = _sampler_for(rows, 1, dev)
+    toks = torch.empty(rows.batch, dtype=torch.int32, device=dev)
+    rng_w = d["rng"].clone()
+
+    def c1(i, rng=d["rng"]):
+        j = i % rows.batch
+        s.sample_rows(d["x"][j:j + 1], d["hist"][j:j + 1], d["counts"][j:j + 1], d["count"][j:j + 1],
+                      rng[j:j + 1], out=toks[j:j + 1])
+    for i in range(max(warmup, 3)):
+        c1(i, rng_w)
+    torch.cuda.synchronize()
+    ms = ev_time(c1, rows.batch)
+    gpu_t = toks.cpu().numpy()
+    ks = _kernel_split(s, lambda: [c1(i, rng_w) for i in range(64)], 64)
+    s.free()
+    ent = {"workload": "batch 1, fp32 N(0,2.5^2) + 8 spikes at +12 (256 distinct rows in turn, 155 MB), "
+                       "64-token window, T=0.6 k=20 p=0.95 min-p=0.05 rep=1.1",
+           "us_per_row": 1e3 * ms, "rows_per_s": 1e3 / ms,
+           "roofline": roofline(1, V * 4 + 64 * 4, ms, "latency (one row)"), "kernel_ms_per_call": ks}
+    if cpu:
+        ent["cpu_baseline"] = cpu_leg(rows.params, rows.logits, rows.hist, rows.hist_counts, rows.hist_count,
+                                      rows.rng, gpu_t, target_s=3.0)
+    out["1"] = ent
+    del d
+
+    # ---- configurations 2 and 3: whole batches, buffers used in turn
+    for name, mk, nbuf, row_bytes, label in (
+            ("2", lambda sd: W.greedy_bf16(B=256, seed=sd), 4, V * 2,
+             "batch 256, bf16 N(0,3^2), 1% rows with duplicate maxima, greedy (4 buffers in turn, 311 MB)"),
+            ("3", lambda sd: W.nucleus_f32(B=64, seed=sd), 8, V * 4 + 128 * 4,
+             "batch 64, fp32 2*Student-t(3), 128-token Zipf(1.1) window, rep 1.2 freq 0.5 pres 0.3, "
+             "top-k off, top-p 0.9, T 0.8 (8 buffers in turn, 311 MB)")):
+        seed0 = int(name)
+        wls = [mk(seed0 + 100 * k) for k in range(nbuf)]
+        ds = [_wl_to_dev(torch, w, dev) for w in wls]
+        B = wls[0].batch
+        s = _sampler_for(wls[0], B, dev)
+        toks = torch.empty(B, dtype=torch.int32, device=dev)
+        rng0 = ds[0]["rng"].clone()
+        s.sample_rows(ds[0]["x"], ds[0]["hist"], ds[0]["counts"], ds[0]["count"], rng0, out=toks)
+        gpu_t = toks.cpu().numpy()
+        rng_w = ds[0]["rng"].clone()
+
+        def cn(i):
+            dd = ds[i % nbuf]
+            s.sample_rows(dd["x"], dd["hist"], dd["counts"], dd["count"], rng_w, out=toks)
+        for i in range(max(warmup, 3)):
+            cn(i)
+        torch.cuda.synchronize()
+        ms = ev_time(cn, steps)
+        ks = _kernel_split(s, lambda: [cn(i) for i in range(steps)], steps)
+        s.free()
+        ent = {"workload": label, "batch": B, "ms_per_step": ms, "rows_per_s": B / (ms * 1e-3),
+               "roofline": roofline(B, row_bytes, ms, "hbm"), "kernel_ms_per_step": ks}
+        if cpu:
+            w0 = wls[0]
+            ent["cpu_baseline"] = cpu_leg(w0.params, w0.logits_f32(), w0.hist if w0.window else None,
+                                          w0.hist_counts if w0.window else None,
+                                          w0.hist_count if w0.window else None, w0.rng, gpu_t,
+                                          target_s=3.0)
+        out[name] = ent
+        del ds
+    torch.cuda.empty_cache()
+    return out
+
+
 def make_inputs(torch, B, seed, device):
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -341,6 +513,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1024, help="rows per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", dest="configs", action="store_false",
+                    help="skip configurations 1-3 (batch 1 fp32, batch 256 greedy, batch 64 nucleus)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-lm-head", dest="lm_head", action="store_false",
                     help="skip the RMSNorm + lm_head measurement")
@@ -410,6 +584,7 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    rng_init = rng.clone()
     for i in range(args.warmup):
         step(i)
     sync_all()
@@ -443,18 +618,29 @@ def main():
     sync_all()
     pr = s.profile_read()
     s.profile(False)
+    kms = {k: pr[k] / args.steps for k in ("stream_ms", "finish_ms", "ties_ms", "emit_ms")}
     row_ms = pr["stream_ms"] / max(pr["row_launches"], 1)  # the streaming pass: every logit once
     hbm, peak_kind = peaks()
-    achieved = B * ROW_BYTES / (row_ms / 1e3) / 1e9
+    stream_ach = B * ROW_BYTES / (row_ms / 1e3) / 1e9
+    step_ach = B * STEP_ROW_BYTES / (ms_step / 1e3) / 1e9
     traffic = None
-    tfile = os.path.join(ROOT, "profiles", "row_stream_kernel_topk_bf16.txt")
+    tfile = os.path.join(ROOT, "profiles", "launches_topk_bf16_b1024.md")
     if os.path.exists(tfile):
         for ln in open(tfile):
-            if ln.startswith("dram_bytes_per_launch_B1024:"):
+            if ln.startswith("dram_bytes_per_step_B1024:"):
                 try:
                     traffic = float(ln.split(":", 1)[1].split()[0])
                 except ValueError:
                     pass
+
+    # ---- the GPU's tokens for buffer 0 from the initial RNG states: checked
+    # against the reference in the CPU-baseline leg below
+    parity_tokens = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rng_p = rng_init.clone()
+        tok_p = torch.empty(B, dtype=torch.int32, device=dev)
+        s.sample_rows(bufs[0][0], hist, counts, count, rng_p, out=tok_p)
+        parity_tokens = tok_p.cpu().numpy()
 
     # ---- end to end through the C ABI with host buffers
     e2e = None
@@ -489,7 +675,7 @@ def main():
                "steps": args.e2e_steps,
                "path": "pinned host -> qs_sample_rows_host (C ABI; tokens and RNG states back) -> host"}
 
-    # ---- the decode tail (final RMSNorm + lm_head, SURVEY configuration 5):
+    # ---- the decode tail (final RMSNorm + lm_head, hidden [128, 1024] bf16):
     # 128 hidden rows x W [151936, 1024] bf16, two weight copies used in turn
     lmh = None
     if rank == 0 and world == 1 and args.lm_head:
@@ -500,9 +686,17 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_reference_sample()
+            from qwen600_engine_b200 import workloads as W
+            cpu = cpu_leg(W.SamplingParams(**PARAMS), bufs[0][0].float().cpu().numpy(),
+                          hist.cpu().numpy(), counts.cpu().numpy(), count.cpu().numpy(),
+                          rng_init.cpu().numpy().view(np.uint64), parity_tokens)
         except Exception as exc:  # report, do not fail the GPU measurement
             cpu = {"value": None, "error": str(exc)}
+
+    configs = None
+    if rank == 0 and world == 1 and args.configs:
+        configs = measure_configs(torch, dev, steps=max(args.steps, 20), warmup=args.warmup,
+                                  cpu=not args.no_cpu_baseline)
 
     if world > 1:
         dist.barrier()
@@ -519,14 +713,18 @@ def main():
                    "parallelism": f"row-sharded x{world}, tokens gathered to rank 0",
                    "l2": "inputs larger than L2: two 311 MB logit buffers used in turn"},
         "e2e": e2e,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": traffic,
-                     "kernel": "qs::row_stream_kernel<bf16>", "kernel_ms": row_ms,
-                     "algorithmic_bytes_per_launch": B * ROW_BYTES, "peak_source": peak_kind,
-                     "step_hbm_frac": world * B * STEP_ROW_BYTES / (ms_step / 1e3) / 1e9 / hbm / world},
-        "kernel_ms_per_step": {k: pr[k] / args.steps for k in ("stream_ms", "finish_ms", "ties_ms", "emit_ms")},
+        "roofline": {"bound": "hbm", "achieved": step_ach, "peak": hbm, "unit": "GB/s",
+                     "frac": step_ach / hbm, "traffic": traffic, "peak_source": peak_kind,
+                     "kernel": "the sampling step (row_stream, row_finish, ties, emit kernels)",
+                     "algorithmic_bytes_per_step": B * STEP_ROW_BYTES,
+                     "stream_pass": {"kernel": "qs::row_stream_kernel<bf16>", "kernel_ms": row_ms,
+                                     "achieved": stream_ach, "frac": stream_ach / hbm,
+                                     "algorithmic_bytes_per_launch": B * ROW_BYTES}},
+        "kernel_ms_per_step": kms,
+        "dominant_kernel": max(kms, key=kms.get).replace("_ms", ""),
         "cpu_baseline": cpu,
         "lm_head": lmh,
+        "configs": configs,
         "clocks": clk.summary(),
         "gpu_launches": launches,
     }

@@ -191,17 +191,18 @@ QS_API int qs_profile_read(qs_sampler* s, qs_profile* out);
  * it serves callers that cannot call cudaMalloc when they sample (code that
  * runs inside a memory pool or allocator it does not own, plugins whose host
  * framework forbids allocation on the decode path, processes that keep their
- * device footprint fixed after start-up).  For each row it applies the
- * penalties of sampler.h:114-141 from the caller's window (as
- * qs_sample_rows) and returns the lowest index of the largest penalised logit
- * (sampler.h:100-111), i.e. temperature-0 sampling; no uniform is drawn.
+ * device footprint fixed after start-up).  It computes the same penalties and
+ * argmax as qs_sample_rows at temperature 0, from the caller's window
+ * (arguments as for qs_sample_rows), and returns the lowest index of the
+ * largest penalised logit; no uniform is drawn.
  * All working memory is one fixed device array inside the library (about
  * 1.1 MB, held by every GPU that loads it until exit): batch <= 1024 and
  * window <= 128, larger requests return QS_ERR_UNSUPPORTED.  The first call on
  * a device looks the array's address up (cudaGetSymbolAddress), so make it
- * before any stream capture.  Calls share the array: calls that overlap on the
- * GPU (unordered streams or threads) race.  Runs on the current device and
- * the given stream (NULL = legacy default stream). */
+ * before any stream capture; after cudaDeviceReset the next call looks it up
+ * again (make that call outside capture too).  Calls share the array: calls
+ * that overlap on the GPU (unordered streams or threads) race.  Runs on the
+ * current device and the given stream (NULL = legacy default stream). */
 QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch, int vocab,
                                  const int* d_hist, const float* d_hist_counts,
                                  const int* d_hist_count, int window,

@@ -2,8 +2,8 @@
 // except the reference's tie arrangement, which qs_ties.cu reproduces when a
 // draw depends on it.
 //
-// Data flow per row (V logits, fp32 or bf16, penalised values substituted
-// from the override table of qs_penalty.cu):
+// Data flow per row (V logits, fp32 or bf16; the window's penalised values
+// are substituted from the override table the streaming pass writes):
 //
 //  A  stream the row once from HBM in 16-byte vector loads (8 in flight per
 //     lane); per segment of 32 lanes x one vector (256 bf16 / 128 fp32
@@ -1368,6 +1368,12 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
             }
             best = warp_min_int(best);
             if (lane == 0) {
+                // sample_argmax starts from logits[0] and compares with a
+                // strict '>': when the penalised logits[0] is NaN no element
+                // compares above it and the reference returns 0 (elsewhere a
+                // NaN is never taken, as fmaxf skips it above)
+                const float l0 = (nov > 0 && ovi[0] == 0) ? ovv[0] : Elem<T>::widen(rv.L[0]);
+                if (!(l0 == l0)) best = 0;
                 out.token = (best == 0x7fffffff) ? 0 : best;
                 out.greedy = 1;
                 res[row] = out;

@@ -54,6 +54,7 @@ static __device__ __align__(256) unsigned char g_static_scratch[sizeof(StaticScr
 constexpr int kMaxDevices = 64;
 static std::mutex g_static_mu;
 static StaticScratch* g_static_ptr[kMaxDevices];  // device address of the array, per device
+static void* g_static_ctx[kMaxDevices];           // the context that address belongs to
 
 }  // namespace qs
 
@@ -62,6 +63,24 @@ using namespace qs;
 extern "C" int qs_static_last_error_set(const char* msg);
 
 namespace {
+// The calling thread's current CUDA context (driver entry point fetched
+// through the runtime, so the library needs no link against libcuda); NULL
+// before the runtime has made one current.
+void* current_context() {
+    typedef int (*CtxGetCurrent)(void**);
+    static CtxGetCurrent fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<CtxGetCurrent>(f);
+    }();
+    void* c = nullptr;
+    if (fn && fn(&c) != 0) c = nullptr;
+    return c;
+}
+
 thread_local char g_static_err[256];
 int static_fail(int code, const char* msg, const char* detail = nullptr) {
     snprintf(g_static_err, sizeof(g_static_err), "%s%s%s", msg, detail ? ": " : "",
@@ -78,6 +97,7 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
                                  const int* d_hist_count, int window, float repetition_penalty,
                                  float frequency_penalty, float presence_penalty, int* d_tokens,
                                  void* stream) {
+    qs_static_last_error_set("");
     if (dtype != QS_F32 && dtype != QS_BF16) return static_fail(QS_ERR_INVALID, "unknown dtype");
     if (!d_logits || !d_tokens) return static_fail(QS_ERR_INVALID, "NULL device pointer");
     if (batch < 0 || batch > kStaticMaxBatch)
@@ -91,20 +111,25 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
     if (batch == 0) return QS_OK;
 
     // Set-up, once per device, with that device current: the array's device
-    // address (in host code its name only stands in for it).
+    // address (in host code its name only stands in for it).  The address
+    // belongs to the device's current context; after cudaDeviceReset the
+    // library's module is loaded again into a new context, so the address is
+    // looked up again when the current context is not the one it came from.
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "cudaGetDevice", cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return static_fail(QS_ERR_UNSUPPORTED, "device ordinal too large");
+    void* ctx = current_context();
     StaticScratch* sc = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_static_mu);
-        if (!g_static_ptr[dev]) {
+        if (!g_static_ptr[dev] || g_static_ctx[dev] != ctx) {
             void* p = nullptr;
             e = cudaGetSymbolAddress(&p, g_static_scratch);
             if (e != cudaSuccess || !p)
                 return static_fail(QS_ERR_CUDA, "cudaGetSymbolAddress", cudaGetErrorString(e));
             g_static_ptr[dev] = reinterpret_cast<StaticScratch*>(p);
+            g_static_ctx[dev] = current_context();  // the lookup made the context current
         }
         sc = g_static_ptr[dev];
     }

@@ -11,7 +11,8 @@ sample() (its final candidate order, renormalised over the kept prefix) and a
 hash of the logits as sample() left them (penalised and temperature-scaled
 in place).
 
-Run (needs the reference tree at /root/reference, via `make -C oracle`):
+Run (needs oracle/_ref/libref_sampler.so, built from the reference tree by
+`make -C oracle REF=<reference tree>`):
     python tests/golden/make_golden.py
 """
 from __future__ import annotations

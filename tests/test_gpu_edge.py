@@ -129,3 +129,54 @@ def test_argument_errors_on_gpu():
     with pytest.raises(SamplerError):
         s.sample_rows(x, rng=rng)                                        # top-k above the limit
     s.free()
+
+
+def test_write_penalized_bit_exact(oracle):
+    """QS_FLAG_WRITE_PENALIZED writes the penalised fp32 logits back in place,
+    as the reference's sample() leaves them after its penalty loop
+    (sampler.h:114-141).  Zipf windows repeat tokens many times, with
+    repetition, frequency and presence penalties all on, so each penalised
+    token replays the whole per-occurrence sequence; every one of the V
+    entries must equal the oracle's bit for bit (the north star allows 1 ulp)."""
+    from qwen600_engine_b200.sampler import QS_FLAG_WRITE_PENALIZED
+    wl = W.nucleus_f32(B=16, seed=31)
+    x0 = wl.logits.copy()
+    g = run_gpu(wl, flags=QS_FLAG_WRITE_PENALIZED)
+    after = g["logits_after"].cpu().numpy()
+    # the oracle at temperature 0 stops after the penalties, so its mutated
+    # rows are the penalised logits alone
+    pen_only = W.SamplingParams(0.0, 1.0, 0.0, 0, wl.params.repetition_penalty,
+                                wl.params.frequency_penalty, wl.params.presence_penalty)
+    o = oracle.sample_rows(pen_only, x0, wl.hist, wl.hist_counts, wl.hist_count,
+                           wl.rng.copy(), want_mutated=True)
+    want = o["mutated"]
+    changed = (want.view(np.uint32) != x0.view(np.uint32)).sum()
+    assert changed > 16 * 50, "the windows should penalise many tokens"
+    diff = np.nonzero(after.view(np.uint32) != want.view(np.uint32))
+    assert diff[0].size == 0, (
+        f"{diff[0].size} penalised logits differ, first at row {diff[0][0]} token {diff[1][0]}: "
+        f"{after[diff[0][0], diff[1][0]]!r} != {want[diff[0][0], diff[1][0]]!r}")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_greedy_nan_first_logit(oracle, dtype):
+    """sample_argmax (sampler.h:100-111) starts from logits[0] with a strict
+    '>': a NaN there wins, anywhere else it never does."""
+    V, B = 3000, 5
+    g = np.random.default_rng(11)
+    x = g.normal(0, 1.0, size=(B, V)).astype(np.float32)
+    x[0, 0] = np.nan                  # reference: token 0
+    x[1, 0] = np.nan
+    x[1, 7] = 50.0                    # still token 0
+    x[2, 5] = np.nan                  # skipped: the argmax of the rest
+    x[3, 0] = -np.inf
+    x[3, 1:] = np.nan                 # token 0
+    x[4, 10] = np.nan
+    x[4, 11] = 9.0
+    logits = W.to_bf16_bits(x) if dtype == "bf16" else x
+    p = W.SamplingParams(0.0, 1.0, 0.0, 0, 1.0, 0.0, 0.0)
+    wl = W._full_window(B, 0, np.zeros(0), 5, "greedy_nan", p, logits, dtype)
+    o = oracle.sample_workload(wl)
+    gg = run_gpu(wl)
+    np.testing.assert_array_equal(gg["tokens"], o["tokens"])
+    assert gg["tokens"][0] == 0 and gg["tokens"][1] == 0 and gg["tokens"][3] == 0

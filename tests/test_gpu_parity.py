@@ -159,6 +159,11 @@ CASES = {
     "greedy_bf16_256": lambda: W.greedy_bf16(B=256),
     "nucleus_f32_24": lambda: W.nucleus_f32(B=24),
     "topk_bf16_192": lambda: W.topk_bf16(B=192),
+    # the measured configurations at their full batch: batch 64 full-vocabulary
+    # nucleus (fp32, Zipf windows with frequency / presence penalties) and the
+    # benchmark's batch 1024 top-k (bf16), where the tie pass queues ~4% of rows
+    "nucleus_f32_64_full": lambda: W.nucleus_f32(B=64),
+    "topk_bf16_1024_full": lambda: W.topk_bf16(B=1024),
 }
 
 

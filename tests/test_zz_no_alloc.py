@@ -35,7 +35,7 @@ def _batch(seed, dtype, B=96, V=W.VOCAB, window=64):
         m = int(np.argmax(x[r]))
         x[r, (m + 12345) % V] = x[r, m]
     hist = g.integers(0, V, size=(B, window)).astype(np.int32)
-    hist[:, :4] = np.argmax(x, axis=1)[:, None]   # penalise each row's maximum, repeatedly
+    hist[:, :min(4, window)] = np.argmax(x, axis=1)[:, None]   # penalise each row's maximum, repeatedly
     counts = g.integers(1, 4, size=(B, window)).astype(np.float32)
     count = np.full(B, window, np.int32)
     logits = W.to_bf16_bits(x) if dtype == "bf16" else x
@@ -79,13 +79,30 @@ def _regular_call(torch, x, h, c, n, pen):
 def test_static_entry_matches_regular_entry_on_consecutive_calls():
     torch = _torch()
     pen = (1.3, 0.4, 0.25)
-    # two calls in a row, different data and dtype, reusing the fixed memory
-    for seed, dtype in ((101, "bf16"), (202, "f32")):
-        d = _dev(torch, *_batch(seed, dtype), dtype)
+    # calls in a row, different data, dtype, batch and window, reusing the
+    # fixed memory: a large call first, then smaller ones, so that results or
+    # window tables a larger call left behind would show
+    cases = ((101, "bf16", 96, 64), (202, "f32", 96, 64), (303, "bf16", 5, 3), (404, "f32", 7, 0))
+    for seed, dtype, B, window in cases:
+        d = _dev(torch, *_batch(seed, dtype, B=B, window=window), dtype)
         got = _static_call(torch, *d, pen)
         want = _regular_call(torch, *d, pen)
-        np.testing.assert_array_equal(got, want)
+        np.testing.assert_array_equal(got, want, err_msg=f"seed {seed} ({dtype}, B={B}, window={window})")
         assert (got >= 0).all()
+
+
+def test_static_entry_allocates_no_device_memory():
+    torch = _torch()
+    pen = (1.2, 0.0, 0.0)
+    d = _dev(torch, *_batch(505, "bf16", B=64, window=32), "bf16")
+    _static_call(torch, *d, pen)            # set-up: the array's address is looked up once
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        _static_call(torch, *d, pen)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"device memory in use grew by {free0 - free1} bytes"
 
 
 def test_static_entry_rejects_sizes_beyond_its_memory():
