@@ -181,11 +181,19 @@ typedef struct {
     long long launches;  /* kernel launch sites passed by this library's calls */
     long long row_launches; /* streaming-pass launches */
     long long timed_calls; /* calls whose kernels were timed */
+    long long tie_clusters; /* clusters the last tie replay launched (rows they share) */
 } qs_profile;
 
 QS_API int qs_profile_enable(qs_sampler* s, int on);
 QS_API int qs_profile_reset(qs_sampler* s);
 QS_API int qs_profile_read(qs_sampler* s, qs_profile* out);
+
+/* Phase clocks for kernel tuning: with phases on, the row kernel records 12
+ * clock64() stamps per row (which = 0) and the tie replay 16 per queued row in
+ * queue order (which = 1) into device buffers that qs_profile_phases_read
+ * copies out (n entries, synchronising the handle's device first). */
+QS_API int qs_profile_phases(qs_sampler* s, int on);
+QS_API int qs_profile_phases_read(qs_sampler* s, int which, long long* host_out, int n);
 
 /* Greedy sampling that allocates nothing.  No counterpart in the reference:
  * it serves callers that cannot call cudaMalloc when they sample (code that

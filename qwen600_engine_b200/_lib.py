@@ -30,6 +30,7 @@ EXPORTS = (
     "qs_set_rng_state", "qs_get_rng_state", "qs_reset_sampler_history", "qs_sample",
     "qs_sample_rows", "qs_sample_rows_debug", "qs_sample_host", "qs_sample_rows_host", "qs_last_error",
     "qs_max_vocab", "qs_profile_enable", "qs_profile_reset", "qs_profile_read",
+    "qs_profile_phases", "qs_profile_phases_read",
     "qs_argmax_rows_static", "qs_lm_head", "qs_lm_head_sample", "qs_lm_head_logits",
     "qs_lm_head_status", "qs_lm_head_shard", "qs_ipc_handle_bytes", "qs_ipc_alloc", "qs_ipc_open",
     "qs_ipc_close", "qs_ipc_free",
@@ -52,7 +53,8 @@ class RowDebug(C.Structure):
 class Profile(C.Structure):
     _fields_ = [("stream_ms", C.c_double), ("finish_ms", C.c_double), ("ties_ms", C.c_double),
                 ("emit_ms", C.c_double), ("calls", C.c_longlong), ("launches", C.c_longlong),
-                ("row_launches", C.c_longlong), ("timed_calls", C.c_longlong)]
+                ("row_launches", C.c_longlong), ("timed_calls", C.c_longlong),
+                ("tie_clusters", C.c_longlong)]
 
 
 ROW_DEBUG_FIELDS = [f for f, _ in RowDebug._fields_]
@@ -88,6 +90,8 @@ def _load() -> C.CDLL:
     lib.qs_profile_enable.argtypes = [vp, i32]
     lib.qs_profile_reset.argtypes = [vp]
     lib.qs_profile_read.argtypes = [vp, P(Profile)]
+    lib.qs_profile_phases.argtypes = [vp, i32]
+    lib.qs_profile_phases_read.argtypes = [vp, i32, P(C.c_longlong), i32]
     lib.qs_argmax_rows_static.argtypes = [vp, i32, i32, i32, vp, vp, vp, i32, C.c_float, C.c_float,
                                           C.c_float, vp, vp]
     lib.qs_lm_head.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp, vp, vp]

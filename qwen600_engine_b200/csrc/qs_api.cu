@@ -1,6 +1,7 @@
 // C ABI of the B200 sampler (include/qwen600_sampler.h): handle lifetime,
 // parameter / RNG / history management and the launch sequence
-//   penalty_kernel -> row_kernel -> ties_kernel -> emit_kernel
+//   row_kernel (chunk scans; each row's last chunk finishes it) ->
+//   select_kernel (rows whose draw depends on the reference's tie order) -> emit_kernel
 // on the caller's stream.  All device memory is allocated in
 // qs_build_sampler; the sampling entry points allocate nothing.
 #include <cuda_bf16.h>
@@ -20,19 +21,16 @@
 namespace qs {
 
 template <typename T>
-cudaError_t launch_row_stream(const T*, int, int, RowParams, RowWindow, RowResult*, RowScratch,
-                              cudaStream_t, long long* phase_cycles = nullptr);
-template <typename T>
-cudaError_t launch_row_finish(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*,
-                              int*, int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t,
-                              long long* phase_cycles = nullptr);
+cudaError_t launch_rows(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*, int*,
+                        int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t,
+                        long long* phase_cycles = nullptr);
 cudaError_t launch_write_penalized(float*, int, int, const int*, const int*, const float*, int,
                                    cudaStream_t);
 template <typename T>
-cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
-                               const int*, const int*, RowResult*, unsigned long long*, int*, int,
-                               int*, float*, int, ExpFix, cudaStream_t,
-                               long long* phase_cycles = nullptr);
+cudaError_t launch_select_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
+                                 const int*, const int*, RowResult*, RowScratch, int*, int*, int, int,
+                                 int*, float*, int, ExpFix, cudaStream_t, long long* phase_cycles,
+                                 long long* clusters_out);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, float*, cudaStream_t);
 template <typename T>
@@ -127,12 +125,18 @@ struct qs_sampler {
     __nv_bfloat16* lh_logits = nullptr;  // [max_batch, vocab]
     int* lh_err = nullptr;
     ExpFix fix() const { return ExpFix{exp_off, exp_ent, exp_bloom, (uint32_t)QS_EXP_NB}; }
-    // the row kernel's hand-over from its streaming to its finishing pass
+    // the row kernel's hand-over from a row's chunk scans to its finishing CTA
     float* rs_segm = nullptr;
-    RowScratch scratch() const { return RowScratch{rs_segm, row_scratch_seg_stride(vocab)}; }
+    int* rs_done = nullptr;                   // [B] chunks scanned
+    unsigned long long* rs_gmax = nullptr;    // [B]
+    RowScratch scratch() const {
+        return RowScratch{rs_segm, row_scratch_seg_stride(vocab), rs_done, rs_gmax};
+    }
     // launch accounting and optional per-kernel event timing
     bool profiling = false;
     qs_profile prof{};
+    long long* ph_row = nullptr;   // [max_batch, 12] row kernel phase clocks (when on)
+    long long* ph_sel = nullptr;   // [max_batch, 16] tie replay phase clocks (when on)
     struct Timed { int kind; cudaEvent_t a, b; };
     std::vector<Timed> pending;
     std::vector<cudaEvent_t> event_pool;
@@ -194,8 +198,8 @@ static void release(qs_sampler* s) {
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts, s->slot_counts,
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
-                    s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm, s->st_hist, s->st_counts,
-                    s->st_count, s->st_rng};
+                    s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm, s->rs_done,
+                    s->rs_gmax, s->st_hist, s->st_counts, s->st_count, s->st_rng, s->ph_row, s->ph_sel};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
@@ -293,6 +297,8 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     ALLOC(s->tie_pos, sizeof(int) * 2 * V * s->tie_ctas);
     ALLOC(s->rng, sizeof(unsigned long long) * B);
     ALLOC(s->rs_segm, sizeof(float) * B * (size_t)row_scratch_seg_stride(vocab));
+    ALLOC(s->rs_done, sizeof(int) * B);
+    ALLOC(s->rs_gmax, sizeof(unsigned long long) * B);
     ALLOC(s->d_in, sizeof(float) * B * V);
     ALLOC(s->st_hist, sizeof(int) * B * (size_t)s->ov_stride);
     ALLOC(s->st_counts, sizeof(float) * B * (size_t)s->ov_stride);
@@ -332,6 +338,8 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
         e = cudaMemcpy(s->exp_bloom, bloom.data(), sizeof(uint32_t) * bloom.size(),
                        cudaMemcpyHostToDevice);
     }
+    if (e == cudaSuccess) e = cudaMemset(s->rs_done, 0, sizeof(int) * B);
+    if (e == cudaSuccess) e = cudaMemset(s->rs_gmax, 0, sizeof(unsigned long long) * B);
     if (e == cudaSuccess && W > 0) {
         e = cudaMemset(s->hcount, 0, sizeof(int) * B);
         if (e == cudaSuccess) e = cudaMemset(s->hpos, 0, sizeof(int) * B);
@@ -493,40 +501,38 @@ static int run(qs_sampler* s, const Call& c) {
     CK(cudaMemsetAsync(s->slow_count, 0, sizeof(int), c.stream));
     RowParams rp{p.temperature, p.topp, p.minp, p.top_k, c.flags};
     {
-    KernelScope ks(s, 0, c.stream);
-    if (c.dtype == QS_F32)
-        CK(launch_row_stream<float>((const float*)c.logits, B, V, rp, win, s->res, s->scratch(), c.stream));
-    else
-        CK(launch_row_stream<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, s->res,
-                                            s->scratch(), c.stream));
-    }
-    if (!greedy) {
-    KernelScope ks(s, 1, c.stream);
-    if (c.dtype == QS_F32) {
-        CK(launch_row_finish<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res,
-                                    s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
-                                    c.cand_cap, s->fix(), s->scratch(), c.stream));
-    } else {
-        CK(launch_row_finish<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng,
-                                            s->res, s->slow_list, s->slow_count, c.cand_index,
-                                            c.cand_prob, c.cand_cap, s->fix(), s->scratch(), c.stream));
-    }
+        KernelScope ks(s, 0, c.stream);
+        if (c.dtype == QS_F32)
+            CK(launch_rows<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res, s->slow_list,
+                                  s->slow_count, c.cand_index, c.cand_prob, c.cand_cap, s->fix(),
+                                  s->scratch(), c.stream, s->ph_row));
+        else
+            CK(launch_rows<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng, s->res,
+                                          s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
+                                          c.cand_cap, s->fix(), s->scratch(), c.stream, s->ph_row));
     }
     if (!greedy && topk && !(c.flags & QS_FLAG_INDEX_TIES)) {
+        // rows whose draw depends on the reference's tie arrangement: the
+        // quick_select replay (one cluster per row; scratch slot per cluster)
         KernelScope ks(s, 2, c.stream);
         TieParams tp{p.temperature, p.topp, p.minp, p.top_k};
-        const int nct = B < s->tie_ctas ? B : s->tie_ctas;
-        if (c.dtype == QS_F32) {
-            CK(launch_ties_kernel<float>((const float*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val,
-                                         s->ov_stride, s->slow_list, s->slow_count, s->res,
-                                         s->tie_scratch, s->tie_pos, nct, c.cand_index, c.cand_prob,
-                                         c.cand_cap, s->fix(), c.stream));
-        } else {
-            CK(launch_ties_kernel<__nv_bfloat16>(
-                (const __nv_bfloat16*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val, s->ov_stride,
-                s->slow_list, s->slow_count, s->res, s->tie_scratch, s->tie_pos, nct, c.cand_index,
-                c.cand_prob, c.cand_cap, s->fix(), c.stream));
-        }
+        int* idx_scratch = reinterpret_cast<int*>(s->tie_scratch);
+        cudaError_t e;
+        if (c.dtype == QS_F32)
+            e = launch_select_kernel<float>((const float*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val,
+                                            s->ov_stride, s->slow_list, s->slow_count, s->res, s->scratch(),
+                                            s->tie_pos, idx_scratch, B, s->tie_ctas, c.cand_index,
+                                            c.cand_prob, c.cand_cap, s->fix(), c.stream, s->ph_sel,
+                                            &s->prof.tie_clusters);
+        else
+            e = launch_select_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, V, tp, ovn, s->ov_idx,
+                                                    s->ov_val, s->ov_stride, s->slow_list, s->slow_count,
+                                                    s->res, s->scratch(), s->tie_pos, idx_scratch, B,
+                                                    s->tie_ctas, c.cand_index, c.cand_prob, c.cand_cap,
+                                                    s->fix(), c.stream, s->ph_sel, &s->prof.tie_clusters);
+        if (e == cudaErrorInvalidValue)
+            return fail(QS_ERR_UNSUPPORTED, "tie replay: vocabulary %d with top_k %d exceeds shared memory", V, p.top_k);
+        CK(e);
     }
     if (!greedy && !(topk && !(c.flags & QS_FLAG_INDEX_TIES))) {
         // rows queued by the row kernel: the full sort (its scratch is the tie
@@ -636,7 +642,41 @@ int qs_profile_reset(qs_sampler* s) {
         s->event_pool.push_back(t.b);
     }
     s->pending.clear();
+    const long long tc = s->prof.tie_clusters;
     s->prof = qs_profile{};
+    s->prof.tie_clusters = tc;
+    return QS_OK;
+}
+
+int qs_profile_phases(qs_sampler* s, int on) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    DeviceGuard dg(s->device);
+    if (on && !s->ph_row) {
+        CK(cudaMalloc(&s->ph_row, sizeof(long long) * 12 * (size_t)s->max_batch));
+        CK(cudaMalloc(&s->ph_sel, sizeof(long long) * 16 * (size_t)s->max_batch));
+        CK(cudaMemset(s->ph_row, 0, sizeof(long long) * 12 * (size_t)s->max_batch));
+        CK(cudaMemset(s->ph_sel, 0, sizeof(long long) * 16 * (size_t)s->max_batch));
+    } else if (!on && s->ph_row) {
+        CK(cudaDeviceSynchronize());
+        cudaFree(s->ph_row);
+        cudaFree(s->ph_sel);
+        s->ph_row = nullptr;
+        s->ph_sel = nullptr;
+    }
+    return QS_OK;
+}
+
+int qs_profile_phases_read(qs_sampler* s, int which, long long* host_out, int n) {
+    g_err.clear();
+    if (!s || !host_out) return fail(QS_ERR_INVALID, "NULL argument");
+    long long* src = which == 0 ? s->ph_row : s->ph_sel;
+    const int cap = (which == 0 ? 12 : 16) * s->max_batch;
+    if (!src) return fail(QS_ERR_INVALID, "phase clocks are off");
+    if (n < 0 || n > cap) return fail(QS_ERR_INVALID, "n %d outside [0, %d]", n, cap);
+    DeviceGuard dg(s->device);
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(host_out, src, sizeof(long long) * n, cudaMemcpyDeviceToHost));
     return QS_OK;
 }
 

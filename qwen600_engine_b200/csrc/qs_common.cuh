@@ -49,12 +49,19 @@ struct LhPeer {
 };
 
 struct RowScratch {
-    float* segm;   // [rows][seg_stride]
+    float* segm;               // [rows][seg_stride] segment maxima (chunk scans -> the row's finish;
+                               // the finish writes back the penalised maxima of window segments)
     int seg_stride;
+    int* done;                 // [rows] chunks scanned; the last one finishes the row, then clears
+                               // done and gmax for the next call
+    unsigned long long* gmax;  // [rows] greedy rows: packed (order key, ~index) of the largest
+                               // logit outside the penalty window
 };
 // Segment maxima per row that fit either element type (fp32 segments are the
 // shorter: 128 elements).
 inline int row_scratch_seg_stride(int V) { return (V + 127) / 128; }
+constexpr int kRowChunkSegs = 64;  // segments per chunk scan (one CTA each)
+inline int row_chunks(int V, int seg) { return ((V + seg - 1) / seg + kRowChunkSegs - 1) / kRowChunkSegs; }
 
 struct TieParams {
     float temperature, topp, minp;

@@ -1092,23 +1092,39 @@ __device__ __noinline__ void finish_by_segments(RowView<T> rv, int nseg, const f
     }
 }
 
-// Streaming pass: the window's penalties, the row's segment maxima and the
-// stash, left in `scr` for row_finish_kernel; greedy rows are finished here.
-// Its shared memory ends where the finishing pass's stash region begins.
+// ------------------------------------------------------------- the row kernel
+// One CTA per chunk of kRowChunkSegs segments of one row (grid: rows x
+// chunks).  Every CTA streams its chunk once from HBM (8 segments in flight
+// per warp) and leaves in global scratch the chunk's raw segment maxima or,
+// for greedy rows, the chunk's largest logit outside the penalty window with
+// its lowest index.  The last CTA of a row to finish (a ticket on the row's
+// counter) finishes the row: the penalty window (sampler.h:114-141), the
+// stash of the elements that may matter to the softmax sum (gathered from
+// the segments the chunks have just streamed, mostly still in L2), the
+// exact softmax denominator, the candidates, min-p / top-p and the draw.
+// Rows thus finish while other rows still stream, and a batch of a few rows
+// still spreads over the whole GPU.
 template <typename T>
-__global__ void __launch_bounds__(kRowThreads, kStreamMinBlocks)
-row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
-                  RowResult* __restrict__ res, RowScratch scr, int ccap, int scap,
-                  long long* __restrict__ phase_cycles) {
+__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
+row_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, RowWindow win,
+           unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
+           int* __restrict__ slow_list, int* __restrict__ slow_count,
+           int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
+           ExpFix fx, int ccap, int scap, RowScratch scr, long long* __restrict__ phase_cycles) {
     constexpr int EPL = Elem<T>::kPerLane;
     constexpr int SEG = 32 * EPL;
-    constexpr int U = kRowRound / kRowWarps;  // segments in flight per warp in the streaming pass
-    const int row = blockIdx.x;
+    constexpr int US = kRowChunkSegs / kRowWarps;  // segments in flight per warp in the scan
+    constexpr int U = 2;  // gathered segments in flight per warp in the finish (more held
+                          // more registers than the 80 the kernel is sized for)
+    const int row = blockIdx.x / nchunk;
+    const int chunk = blockIdx.x - row * nchunk;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const RowSmem L(V, SEG, win.window, ccap, scap);
     const int nseg = L.nseg;
+    const bool greedy = prm.temperature < 1e-6f;
+    const float inv = greedy ? 1.0f : __fdiv_rn(1.0f, prm.temperature);
 
-    // ---- shared memory carve-up
+    // ---- shared memory carve-up (the finish's layout; the scan uses little)
     extern __shared__ __align__(16) unsigned char smem[];
     float* segm = (float*)(smem + L.segm);            // segment maxima (l, then t)
     uint32_t* segk = (uint32_t*)(smem + L.segk);      // order keys of segm (t)
@@ -1118,17 +1134,26 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     int* ofirst = (int*)(smem + L.ofirst);
     unsigned long long* pairs = (unsigned long long*)(smem + L.pairs);
     float* pcnt = (float*)(smem + L.pcnt);
-    uint32_t* pubr = (uint32_t*)(smem + L.pubr);      // per streaming round: max key seen
     float* rawv = (float*)(smem + L.rawv);            // window tokens' raw logits
     int* rech = (int*)(smem + L.rech);                // segments whose maximum is recomputed
+    unsigned char* region = smem + L.region;          // stash, or the dense method's tables
+    float* st_t = (float*)region;
+    int* st_i = (int*)(region + 4 * (size_t)scap);
+    float* st_e = (float*)(region + 8 * (size_t)scap);   // expf(t - max), the reference's term
+    float* slist = (float*)(region + 12 * (size_t)scap); // terms in index order
+    int* sstart = (int*)(region + 16 * (size_t)scap);
+    int* scnt = sstart + nseg;
+    const Cands cd{(float*)(smem + L.ct), (int*)(smem + L.ci), (float*)(smem + L.cp),
+                   (int*)(smem + L.so), (unsigned long long*)(smem + L.ck),
+                   (uint32_t*)(smem + L.rhist), ccap};
     __shared__ RowShared sh;
+    __shared__ uint32_t cwin[kRowChunkSegs / 32];  // chunk segments holding a window token
+    __shared__ unsigned long long cbest;         // greedy: packed (key, ~index) of the chunk's maximum
+    __shared__ int cnw, clast;
+    const RowOut ro{res, slow_list, slow_count, cand_index_out, cand_prob_out, cand_cap, row};
 
     long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
     auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
-    stamp(0);
-
-    const bool greedy = prm.temperature < 1e-6f;
-    const float inv = greedy ? 1.0f : __fdiv_rn(1.0f, prm.temperature);
 
     RowView<T> rv;
     rv.L = logits + (size_t)row * V;
@@ -1138,79 +1163,128 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     rv.ovi = ovi;
     rv.ovv = ovv;
     rv.nov = 0;
-    // the streaming pass keeps one round of vectors in flight per warp
-    uint4 r[U];
-    auto request = [&](int jj) {
-        const int gb = jj * kRowRound + warp;
+
+    // ---- the chunk scan: every vector of the chunk in flight at once
+    const int g0 = chunk * kRowChunkSegs;
+    uint4 rs[US];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int g = gb + u * kRowWarps;
-            if ((g < nseg) && rv.full(g, lane)) r[u] = rv.raw(g, lane);
-            else r[u] = make_uint4(0u, 0u, 0u, 0u);
-        }
-    };
-    request(0);
-    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.maxlb = fkey(-INFINITY); sh.misc[6] = 0; sh.misc[7] = 0; }
-    for (int g = tid; g < nseg; g += kRowThreads) segov[g] = 0;
-    // the window's slots, their counts and the row's slot count travel to
-    // shared memory while the row streams (asynchronous copies hold no
-    // registers); the slots are staged in ofirst, rebuilt from them later
+    for (int u = 0; u < US; u++) {
+        const int g = g0 + warp + u * kRowWarps;
+        rs[u] = (g < nseg && rv.full(g, lane)) ? rv.raw(g, lane) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    // the window's tokens in this chunk, read while the chunk streams
+    int* ctok = ofirst;  // greedy: this chunk's window tokens (room for the whole window)
+    if (tid < kRowChunkSegs / 32) cwin[tid] = 0u;
+    if (tid == 0) { cnw = 0; cbest = 0ull; }
+    __syncthreads();
     const bool pen_possible = win.hist && win.count && (win.rp != 1.0f || win.fp != 0.0f || win.pp != 0.0f);
     if (pen_possible) {
-        for (int i = tid; i < win.window; i += kRowThreads) {
-            cp_async4(ofirst + i, win.hist + (size_t)row * win.window + i);
-            if (win.slot_counts) cp_async4(pcnt + i, win.slot_counts + (size_t)row * win.window + i);
-        }
-        if (tid == 0) cp_async4(&sh.misc[5], win.count + row);
-        cp_async_commit();
-    }
-    stamp(1);
-
-    // ---- A: streaming pass: the maximum of each segment of the raw logits
-    // (the penalty window is applied after the pass).  r holds this round's
-    // vectors; the next round's are requested as soon as this round's maxima
-    // are taken.
-    for (int j = 0; j < L.nrounds; j++) {
-        const int g0 = j * kRowRound + warp;
-        unsigned slow = 0;  // partial segments (warp-uniform)
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int g = g0 + u * kRowWarps;
-            if (g < nseg) {
-                if (rv.aligned && (g + 1) * SEG <= V) {
-                    const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(vec_max<T>(r[u])));
-                    if (lane == 0) segm[g] = fkey_inv(km);
-                } else {
-                    slow |= 1u << u;
+        int cntw = win.count[row];
+        cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
+        for (int i = tid; i < cntw; i += kRowThreads) {
+            const int t = win.hist[(size_t)row * win.window + i];
+            if (t >= 0 && t < V) {
+                const int j = t / SEG - g0;
+                if (j >= 0 && j < kRowChunkSegs) {
+                    atomicOr(&cwin[j >> 5], 1u << (j & 31));
+                    if (greedy) ctok[atomicAdd(&cnw, 1)] = t;
                 }
             }
         }
-        while (slow) {
-            const int u = __ffs(slow) - 1;
-            slow &= slow - 1;
-            const int g = g0 + u * kRowWarps;
-            // the segment's vector is still in r[u]; partial lanes read -inf
-            // past the row
-            uint4 ru = r[0];
-#pragma unroll
-            for (int q = 1; q < U; q++)
-                if (q == u) ru = r[q];
-            float v[EPL];
-            rv.widen_raw(g, lane, rv.full(g, lane), ru, v);
-            float m = v[0];
-#pragma unroll
-            for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
-            const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
-            if (lane == 0) segm[g] = fkey_inv(km);
-        }
-        if (j + 1 < L.nrounds) request(j + 1);  // r is free: every maximum of this round is taken
     }
-    if (pen_possible) cp_async_wait_all();
     __syncthreads();
-
+    if (greedy) {
+        // the largest logit of each segment outside the window, lowest index
+        // first (sample_argmax's strict '>', sampler.h:100-111; NaN never
+        // taken; -0 and +0 compare equal)
+        const int nw = cnw;
+#pragma unroll
+        for (int u = 0; u < US; u++) {
+            const int g = g0 + warp + u * kRowWarps;
+            if (g >= nseg) continue;  // warp-uniform
+            const int j = g - g0;
+            const bool wseg = (cwin[j >> 5] >> (j & 31)) & 1u;
+            float v[EPL];
+            rv.widen_raw(g, lane, rv.full(g, lane), rs[u], v);
+            float bm = 0.0f;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const int idx = g * SEG + lane * EPL + e;
+                const float x = v[e];
+                bool ok = idx < V && x == x;
+                if (ok && wseg)
+                    for (int k = 0; k < nw; k++) ok = ok && ctok[k] != idx;
+                if (ok && (bi == 0x7fffffff || x > bm)) { bm = x; bi = idx; }
+            }
+            unsigned long long key = 0ull;
+            if (bi != 0x7fffffff)
+                key = ((unsigned long long)fkey(bm == 0.0f ? 0.0f : bm) << 32) | (unsigned long long)(~(uint32_t)bi);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, o);
+                key = y > key ? y : key;
+            }
+            if (lane == 0 && key) atomicMax(&cbest, key);
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < US; u++) {
+            const int g = g0 + warp + u * kRowWarps;
+            if (g >= nseg) continue;  // warp-uniform
+            float m;
+            if (rv.aligned && (g + 1) * SEG <= V) {
+                m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(vec_max<T>(rs[u]))));
+            } else {
+                float v[EPL];
+                rv.widen_raw(g, lane, rv.full(g, lane), rs[u], v);
+                float lm2 = v[0];
+#pragma unroll
+                for (int e = 1; e < EPL; e++) lm2 = fmaxf(lm2, v[e]);
+                m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(lm2)));
+            }
+            if (lane == 0) scr.segm[(size_t)row * scr.seg_stride + g] = m;
+        }
+        if (lane == 0) __threadfence();  // the segment maxima before the row's ticket
+    }
+    // ---- the last chunk of the row to finish finishes the row
+    __syncthreads();
+    if (tid == 0) {
+        if (greedy && cbest) atomicMax(scr.gmax + row, cbest);
+        __threadfence();
+        clast = atomicAdd(scr.done + row, 1) == nchunk - 1;
+    }
+    __syncthreads();
+    if (!clast) return;
+    __threadfence();
+    stamp(0);
+    if (tid == 0) {
+        if (greedy) cbest = __ldcg(scr.gmax + row);
+        // clear the row's counters for the next call (no other CTA of this
+        // call touches them again)
+        scr.done[row] = 0;
+        scr.gmax[row] = 0ull;
+        sh.nst = 0; sh.ovf = 0; sh.nhot = 0; sh.maxlb = fkey(-INFINITY);
+        sh.misc[6] = 0; sh.misc[7] = 0;
+        int c5 = pen_possible ? win.count[row] : 0;
+        sh.misc[5] = c5 < 0 ? 0 : (c5 > win.window ? win.window : c5);
+    }
+    // the window's slots and their counts
+    if (pen_possible) {
+        for (int i = tid; i < win.window; i += kRowThreads) {
+            ofirst[i] = win.hist[(size_t)row * win.window + i];
+            pcnt[i] = win.slot_counts ? win.slot_counts[(size_t)row * win.window + i] : 0.0f;
+        }
+    }
+    for (int g = tid; g < nseg; g += kRowThreads) {
+        segov[g] = 0;
+        scnt[g] = 0;
+        if (!greedy) segm[g] = __ldcg(scr.segm + (size_t)row * scr.seg_stride + g);
+    }
+    __syncthreads();
     // ---- the row's penalty window (sampler.h:114-141): slots sorted by
     // (token, slot), distinct tokens and the slot range of each
-    int cntw = pen_possible ? sh.misc[5] : 0;
+    int cntw = pen_possible ? sh.misc[5] : 0;  // (clamped again: the slot count is the caller's)
     cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
     const bool pen_on = cntw > 0;
     int nov = 0;
@@ -1311,7 +1385,7 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         // where a NaN or a zero is involved (fmaxf and the order keys may
         // pick differently there), the segment is recomputed below with the
         // penalised values substituted, as the streaming pass would have.
-        for (int j = tid; j < nov; j += kRowThreads) {
+        for (int j = tid; j < nov && !greedy; j += kRowThreads) {
             const int g = ovi[j] / SEG;
             if (j > 0 && ovi[j - 1] / SEG == g) continue;
             const float sraw = segm[g];
@@ -1329,7 +1403,7 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     }
     if (tid == 0 && win.ov_n) win.ov_n[row] = nov;
     rv.nov = nov;
-    for (int i = warp; i < sh.misc[6]; i += kRowWarps) {
+    for (int i = warp; i < sh.misc[6] && !greedy; i += kRowWarps) {
         const int g = rech[i];
         float v[EPL];
         rv.load(g, lane, v);
@@ -1340,123 +1414,46 @@ row_stream_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         if (lane == 0) segm[g] = fkey_inv(km);
     }
     __syncthreads();
-    float lm = -INFINITY;
-    for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
-    const float maxl = rblock_max(lm, sh.red_f);
-    stamp(2);
-
-    RowResult out;
-    out.token = 0; out.greedy = 0; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
-    out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0; out.max_logit = maxl;
-    out.sum = 0.f; out.r = 0.f; out.renorm_sum = 0.f; out.inv_temp = 0.f; out.sum_inv = 0.f;
-    out.status = 0; out.pad_ = 0;
-
-    // ---- greedy: lowest index of the maximum penalised logit
+    stamp(1);
+    // the penalised maxima of the window's segments back to the scratch (the
+    // tie pass bounds the top k by the segment maxima)
+    if (!greedy)
+        for (int j = tid; j < nov; j += kRowThreads) {
+            const int g = ovi[j] / SEG;
+            if (j == 0 || ovi[j - 1] / SEG != g) scr.segm[(size_t)row * scr.seg_stride + g] = segm[g];
+        }
     if (greedy) {
-        int first = 0x7fffffff;
-        for (int g = tid; g < nseg; g += kRowThreads)
-            if (segm[g] == maxl) first = min(first, g);
-        first = rblock_min_int(first, sh.red_i);
-        if (warp == 0) {
-            int best = 0x7fffffff;
-            if (first != 0x7fffffff) {
-                float v[EPL];
-                rv.load(first, lane, v);
-#pragma unroll
-                for (int e = EPL - 1; e >= 0; e--)
-                    if (v[e] == maxl) best = first * SEG + lane * EPL + e;
+        // the window tokens' penalised values against the largest logit
+        // outside the window (lowest index first among equal values)
+        for (int j = tid; j < nov; j += kRowThreads) {
+            const float x = ovv[j];
+            if (x == x) {
+                const unsigned long long key =
+                    ((unsigned long long)fkey(x == 0.0f ? 0.0f : x) << 32) | (unsigned long long)(~(uint32_t)ovi[j]);
+                atomicMax(&cbest, key);
             }
-            best = warp_min_int(best);
-            if (lane == 0) {
-                // sample_argmax starts from logits[0] and compares with a
-                // strict '>': when the penalised logits[0] is NaN no element
-                // compares above it and the reference returns 0 (elsewhere a
-                // NaN is never taken, as fmaxf skips it above)
-                const float l0 = (nov > 0 && ovi[0] == 0) ? ovv[0] : Elem<T>::widen(rv.L[0]);
-                if (!(l0 == l0)) best = 0;
-                out.token = (best == 0x7fffffff) ? 0 : best;
-                out.greedy = 1;
-                res[row] = out;
-            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned long long best = cbest;
+            int token = best ? (int)(~(uint32_t)(best & 0xFFFFFFFFull)) : 0;
+            // sample_argmax starts from logits[0] and compares with a strict
+            // '>': when the penalised logits[0] is NaN no element compares
+            // above it and the reference returns 0
+            const float l0 = (nov > 0 && ovi[0] == 0) ? ovv[0] : Elem<T>::widen(rv.L[0]);
+            if (!(l0 == l0)) token = 0;
+            RowResult out;
+            out.token = (token >= 0 && token < V) ? token : 0;
+            out.greedy = 1; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
+            out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0;
+            out.max_logit = best ? fkey_inv((uint32_t)(best >> 32)) : l0;
+            out.sum = 0.f; out.r = 0.f; out.renorm_sum = 0.f; out.inv_temp = 0.f; out.sum_inv = 0.f;
+            out.status = 0; out.pad_ = 0;
+            res[row] = out;
         }
         return;
     }
 
-    // ---- hand over to the finishing pass
-    for (int g = tid; g < nseg; g += kRowThreads) scr.segm[(size_t)row * scr.seg_stride + g] = segm[g];
-    stamp(11);
-}
-
-// Finishing pass (non-greedy rows): the exact softmax denominator, the
-// candidates, min-p / top-p and the draw, from what row_stream_kernel left in
-// `scr`; rows it cannot settle go to the exact passes.
-template <typename T>
-__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
-row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
-                  unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
-                  int* __restrict__ slow_list, int* __restrict__ slow_count,
-                  int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
-                  ExpFix fx, int ccap, int scap, RowScratch scr, long long* __restrict__ phase_cycles) {
-    constexpr int EPL = Elem<T>::kPerLane;
-    constexpr int SEG = 32 * EPL;
-    // gathered segments in flight per warp: 2 (more held more registers than
-    // the 80 this pass is sized for: at 8 the pass ran ~14% slower, at 4 ~4%)
-    constexpr int U = 2;
-    const int row = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const RowSmem L(V, SEG, win.window, ccap, scap);
-    const int nseg = L.nseg;
-
-    // ---- shared memory carve-up
-    extern __shared__ __align__(16) unsigned char smem[];
-    float* segm = (float*)(smem + L.segm);            // segment maxima (l, then t)
-    uint32_t* segk = (uint32_t*)(smem + L.segk);      // order keys of segm (t)
-    unsigned char* segov = smem + L.segov;
-    int* ovi = (int*)(smem + L.ovi);
-    float* ovv = (float*)(smem + L.ovv);
-    unsigned char* region = smem + L.region;          // stash, or the dense method's tables
-    float* st_t = (float*)region;
-    int* st_i = (int*)(region + 4 * (size_t)scap);
-    float* st_e = (float*)(region + 8 * (size_t)scap);   // expf(t - max), the reference's term
-    float* slist = (float*)(region + 12 * (size_t)scap); // terms in index order
-    int* sstart = (int*)(region + 16 * (size_t)scap);
-    int* scnt = sstart + nseg;
-    const Cands cd{(float*)(smem + L.ct), (int*)(smem + L.ci), (float*)(smem + L.cp),
-                   (int*)(smem + L.so), (unsigned long long*)(smem + L.ck),
-                   (uint32_t*)(smem + L.rhist), ccap};
-    __shared__ RowShared sh;
-    const RowOut ro{res, slow_list, slow_count, cand_index_out, cand_prob_out, cand_cap, row};
-
-    long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
-    auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
-    stamp(10);
-    const float inv = __fdiv_rn(1.0f, prm.temperature);
-
-    // ---- what the streaming pass left: segment maxima; the window's
-    // overrides from the tables it wrote
-    const int nov = (win.ov_n && win.ov_idx) ? win.ov_n[row] : 0;
-    for (int g = tid; g < nseg; g += kRowThreads) {
-        segm[g] = scr.segm[(size_t)row * scr.seg_stride + g];
-        segov[g] = 0;
-        scnt[g] = 0;
-    }
-    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.nhot = 0; sh.maxlb = fkey(-INFINITY); }
-    __syncthreads();
-    for (int j = tid; j < nov; j += kRowThreads) {
-        const int q = win.ov_idx[(size_t)row * win.ov_stride + j];
-        ovi[j] = q;
-        ovv[j] = win.ov_val[(size_t)row * win.ov_stride + j];
-        segov[q / SEG] = 1;
-    }
-    __syncthreads();
-    RowView<T> rv;
-    rv.L = logits + (size_t)row * V;
-    rv.V = V;
-    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
-    rv.segov = segov;
-    rv.ovi = ovi;
-    rv.ovv = ovv;
-    rv.nov = nov;
     float lm = -INFINITY;
     for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
     const float maxl = rblock_max(lm, sh.red_f);
@@ -1494,97 +1491,98 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         }
         __syncthreads();
     }
-    // the largest threshold used (+ 17.5): the stash holds every t >= lbmax - 17.5
-    float lbmax = nseg > 1 ? pre[nseg - 1] : -INFINITY;
-    int* hot = reinterpret_cast<int*>(smem + L.hotl);  // the segments to gather, in any order
-    uint4 r[U];
-    for (int g = tid; g < nseg; g += kRowThreads)
-        if (g == 0 || __fmul_rn(segm[g], inv) >= __fsub_rn(pre[g], kSigGap)) hot[atomicAdd(&sh.nhot, 1)] = g;
-    __syncthreads();
-    const int nhot = sh.nhot;
-    // every gathered segment's lines requested into L2 at once (4 per segment),
-    // so the gather's batches after the first find them there
-    for (int q = tid; q < 4 * nhot; q += kRowThreads)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(rv.L + (size_t)hot[q >> 2] * SEG) + (q & 3) * 128));
-    for (int h0 = warp; h0 < nhot; h0 += U * kRowWarps) {
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int h = h0 + u * kRowWarps;
-            r[u] = make_uint4(0u, 0u, 0u, 0u);
-            if (h < nhot && rv.full(hot[h], lane)) r[u] = rv.raw(hot[h], lane);
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int h = h0 + u * kRowWarps;
-            if (h >= nhot) continue;
-            const int g = hot[h];
-            if (*(volatile int*)&sh.ovf) continue;  // the dense method takes over; stop stashing
-            float v[EPL];
-            rv.widen(g, lane, rv.full(g, lane), r[u], v);
-            float the[EPL];  // each element's threshold
-            const float th = __fsub_rn(pre[g], kSigGap);
-#pragma unroll
-            for (int e = 0; e < EPL; e++) { v[e] = __fmul_rn(v[e], inv); the[e] = th; }
-            if (g == 0) {
-                // the first segment: each element against the running maximum
-                // of the elements before it
-                float run = -INFINITY;
-#pragma unroll
-                for (int e = 0; e < EPL; e++) { the[e] = run; run = fmaxf(run, v[e]); }
-                float x = run;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const float y = __shfl_up_sync(0xffffffffu, x, o);
-                    if (lane >= o) x = fmaxf(x, y);
-                }
-                float before = __shfl_up_sync(0xffffffffu, x, 1);
-                if (lane == 0) before = -INFINITY;
-#pragma unroll
-                for (int e = 0; e < EPL; e++) the[e] = fmaxf(before, the[e]);
-                lbmax = fmaxf(lbmax, __shfl_sync(0xffffffffu, the[EPL - 1], 31));
-#pragma unroll
-                for (int e = 0; e < EPL; e++) the[e] = __fsub_rn(the[e], kSigGap);
+    {
+        // the largest threshold used (+ 17.5): the stash holds every t >= lbmax - 17.5
+        float lbmax = nseg > 1 ? pre[nseg - 1] : -INFINITY;
+        int* hot = reinterpret_cast<int*>(smem + L.hotl);  // the segments to gather, in any order
+        uint4 r[U];
+        for (int g = tid; g < nseg; g += kRowThreads)
+            if (g == 0 || __fmul_rn(segm[g], inv) >= __fsub_rn(pre[g], kSigGap)) hot[atomicAdd(&sh.nhot, 1)] = g;
+        __syncthreads();
+        const int nhot = sh.nhot;
+        // every gathered segment's lines requested into L2 at once (4 per segment),
+        // so the gather's batches after the first find them there
+        for (int q = tid; q < 4 * nhot; q += kRowThreads)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(rv.L + (size_t)hot[q >> 2] * SEG) + (q & 3) * 128));
+        for (int h0 = warp; h0 < nhot; h0 += U * kRowWarps) {
+    #pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int h = h0 + u * kRowWarps;
+                r[u] = make_uint4(0u, 0u, 0u, 0u);
+                if (h < nhot && rv.full(hot[h], lane)) r[u] = rv.raw(hot[h], lane);
             }
-            unsigned keep = 0;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) {
-                const bool kk = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
-                keep |= (kk ? 1u : 0u) << e;
-            }
-            // the kept elements' places in index order: one ballot per slot of
-            // the lanes' vectors (independent, no scan chain)
-            const unsigned lt = (1u << lane) - 1u;
-            int before = 0, tot = 0;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) {
-                const unsigned be = __ballot_sync(0xffffffffu, (keep >> e) & 1u);
-                before += __popc(be & lt);
-                tot += __popc(be);
-            }
-            if (tot == 0) continue;
-            int base = 0;
-            if (lane == 0) base = atomicAdd(&sh.nst, tot);
-            base = __shfl_sync(0xffffffffu, base, 0);
-            if (base + tot <= scap) {
-                if (lane == 0) { sstart[g] = base; scnt[g] = tot; }
-                int pos = base + before;
-#pragma unroll
-                for (int e = 0; e < EPL; e++) {
-                    if ((keep >> e) & 1u) {
-                        st_t[pos] = v[e];
-                        st_i[pos] = g * SEG + lane * EPL + e;
-                        pos++;
+    #pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int h = h0 + u * kRowWarps;
+                if (h >= nhot) continue;
+                const int g = hot[h];
+                if (*(volatile int*)&sh.ovf) continue;  // the dense method takes over; stop stashing
+                float v[EPL];
+                rv.widen(g, lane, rv.full(g, lane), r[u], v);
+                float the[EPL];  // each element's threshold
+                const float th = __fsub_rn(pre[g], kSigGap);
+    #pragma unroll
+                for (int e = 0; e < EPL; e++) { v[e] = __fmul_rn(v[e], inv); the[e] = th; }
+                if (g == 0) {
+                    // the first segment: each element against the running maximum
+                    // of the elements before it
+                    float run = -INFINITY;
+    #pragma unroll
+                    for (int e = 0; e < EPL; e++) { the[e] = run; run = fmaxf(run, v[e]); }
+                    float x = run;
+    #pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const float y = __shfl_up_sync(0xffffffffu, x, o);
+                        if (lane >= o) x = fmaxf(x, y);
                     }
+                    float before = __shfl_up_sync(0xffffffffu, x, 1);
+                    if (lane == 0) before = -INFINITY;
+    #pragma unroll
+                    for (int e = 0; e < EPL; e++) the[e] = fmaxf(before, the[e]);
+                    lbmax = fmaxf(lbmax, __shfl_sync(0xffffffffu, the[EPL - 1], 31));
+    #pragma unroll
+                    for (int e = 0; e < EPL; e++) the[e] = __fsub_rn(the[e], kSigGap);
                 }
-            } else if (lane == 0) {
-                sh.ovf = 1;
+                unsigned keep = 0;
+    #pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    const bool kk = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
+                    keep |= (kk ? 1u : 0u) << e;
+                }
+                // the kept elements' places in index order: one ballot per slot of
+                // the lanes' vectors (independent, no scan chain)
+                const unsigned lt = (1u << lane) - 1u;
+                int before = 0, tot = 0;
+    #pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    const unsigned be = __ballot_sync(0xffffffffu, (keep >> e) & 1u);
+                    before += __popc(be & lt);
+                    tot += __popc(be);
+                }
+                if (tot == 0) continue;
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&sh.nst, tot);
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (base + tot <= scap) {
+                    if (lane == 0) { sstart[g] = base; scnt[g] = tot; }
+                    int pos = base + before;
+    #pragma unroll
+                    for (int e = 0; e < EPL; e++) {
+                        if ((keep >> e) & 1u) {
+                            st_t[pos] = v[e];
+                            st_i[pos] = g * SEG + lane * EPL + e;
+                            pos++;
+                        }
+                    }
+                } else if (lane == 0) {
+                    sh.ovf = 1;
+                }
             }
         }
+        if (lane == 0) atomicMax(&sh.maxlb, fkey(lbmax));
+        __syncthreads();
     }
-    if (lane == 0) atomicMax(&sh.maxlb, fkey(lbmax));
-    __syncthreads();
-
-
+    stamp(2);
     RowResult out;
     out.token = 0; out.greedy = 0; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
     out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0; out.max_logit = maxl;
@@ -1801,74 +1799,42 @@ int row_kernel_ccap(int top_k, int V) {
     return c;
 }
 
-// The streaming pass (every call) and the finishing pass (non-greedy
-// calls), launched separately so callers can time them apart.  `scr` must
-// hold `B` rows of row_scratch_seg_stride(V) segment maxima unless the call
-// is greedy.
+// The row kernel over `B` rows: rows x chunks CTAs.  `scr` holds per row
+// row_scratch_seg_stride(V) segment maxima and the two counters (zero before
+// the first call; each row's finishing CTA clears them again).  Greedy calls
+// use only the counters.
 template <typename T>
-cudaError_t launch_row_stream(const T* logits, int B, int V, RowParams prm, RowWindow win, RowResult* res,
-                              RowScratch scr, cudaStream_t stream, long long* phase_cycles) {
+cudaError_t launch_rows(const T* logits, int B, int V, RowParams prm, RowWindow win,
+                        unsigned long long* rng, RowResult* res, int* slow_list, int* slow_count,
+                        int* cand_index, float* cand_prob, int cand_cap, ExpFix fx, RowScratch scr,
+                        cudaStream_t stream, long long* phase_cycles) {
+    if (B <= 0) return cudaSuccess;
     const int ccap = row_kernel_ccap(prm.top_k, V);
     if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
     const bool greedy = prm.temperature < 1e-6f;
-    if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V))) return cudaErrorInvalidValue;
-    const RowSmem L(V, 32 * (16 / (int)sizeof(T)), win.window, ccap, kStashCap);
-    cudaError_t err = cudaFuncSetAttribute(row_stream_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)L.stream_total);
-    if (err != cudaSuccess) return err;
-    row_stream_kernel<T><<<B, kRowThreads, L.stream_total, stream>>>(logits, V, prm, win, res, scr, ccap,
-                                                               kStashCap, phase_cycles);
-    return cudaGetLastError();
-}
-
-template <typename T>
-cudaError_t launch_row_finish(const T* logits, int B, int V, RowParams prm, RowWindow win,
-                              unsigned long long* rng, RowResult* res, int* slow_list, int* slow_count,
-                              int* cand_index, float* cand_prob, int cand_cap, ExpFix fx, RowScratch scr,
-                              cudaStream_t stream, long long* phase_cycles) {
-    const int ccap = row_kernel_ccap(prm.top_k, V);
-    if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
-    if (prm.temperature < 1e-6f) return cudaSuccess;  // greedy rows are finished by the streaming pass
-    if (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V)) return cudaErrorInvalidValue;
-    const RowSmem L(V, 32 * (16 / (int)sizeof(T)), win.window, ccap, kStashCap);
-    cudaError_t err = cudaFuncSetAttribute(row_finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (!scr.done || !scr.gmax) return cudaErrorInvalidValue;
+    if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V)))
+        return cudaErrorInvalidValue;
+    constexpr int SEG = 32 * (16 / (int)sizeof(T));
+    const RowSmem L(V, SEG, win.window, ccap, kStashCap);
+    cudaError_t err = cudaFuncSetAttribute(row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)L.total);
     if (err != cudaSuccess) return err;
-    row_finish_kernel<T><<<B, kRowThreads, L.total, stream>>>(logits, V, prm, win, rng, res, slow_list,
-                                                              slow_count, cand_index, cand_prob, cand_cap,
-                                                              fx, ccap, kStashCap, scr, phase_cycles);
+    const int nchunk = row_chunks(V, SEG);
+    const long long grid = (long long)B * nchunk;
+    if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+    row_kernel<T><<<(unsigned)grid, kRowThreads, L.total, stream>>>(
+        logits, V, nchunk, prm, win, rng, res, slow_list, slow_count, cand_index, cand_prob, cand_cap,
+        fx, ccap, kStashCap, scr, phase_cycles);
     return cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t launch_row_kernel(const T* logits, int B, int V, RowParams prm, RowWindow win,
-                              unsigned long long* rng, RowResult* res, int* slow_list,
-                              int* slow_count, int* cand_index, float* cand_prob, int cand_cap,
-                              ExpFix fx, RowScratch scr, cudaStream_t stream, long long* phase_cycles) {
-    cudaError_t err = launch_row_stream<T>(logits, B, V, prm, win, res, scr, stream, phase_cycles);
-    if (err != cudaSuccess) return err;
-    return launch_row_finish<T>(logits, B, V, prm, win, rng, res, slow_list, slow_count, cand_index,
-                                cand_prob, cand_cap, fx, scr, stream, phase_cycles);
-}
-
-template cudaError_t launch_row_kernel<float>(const float*, int, int, RowParams, RowWindow,
-                                              unsigned long long*, RowResult*, int*, int*, int*,
-                                              float*, int, ExpFix, RowScratch, cudaStream_t, long long*);
-template cudaError_t launch_row_kernel<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams,
-                                                      RowWindow, unsigned long long*, RowResult*,
-                                                      int*, int*, int*, float*, int, ExpFix, RowScratch,
-                                                      cudaStream_t, long long*);
-template cudaError_t launch_row_stream<float>(const float*, int, int, RowParams, RowWindow, RowResult*,
-                                              RowScratch, cudaStream_t, long long*);
-template cudaError_t launch_row_stream<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
-                                                      RowResult*, RowScratch, cudaStream_t, long long*);
-template cudaError_t launch_row_finish<float>(const float*, int, int, RowParams, RowWindow,
-                                              unsigned long long*, RowResult*, int*, int*, int*, float*,
-                                              int, ExpFix, RowScratch, cudaStream_t, long long*);
-template cudaError_t launch_row_finish<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
-                                                      unsigned long long*, RowResult*, int*, int*, int*,
-                                                      float*, int, ExpFix, RowScratch, cudaStream_t,
-                                                      long long*);
+template cudaError_t launch_rows<float>(const float*, int, int, RowParams, RowWindow, unsigned long long*,
+                                        RowResult*, int*, int*, int*, float*, int, ExpFix, RowScratch,
+                                        cudaStream_t, long long*);
+template cudaError_t launch_rows<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
+                                                unsigned long long*, RowResult*, int*, int*, int*, float*,
+                                                int, ExpFix, RowScratch, cudaStream_t, long long*);
 
 // QS_FLAG_WRITE_PENALIZED: the reference's in-place penalty update of fp32
 // logits (sampler.h:114-141), written after every pass has read the raw row.

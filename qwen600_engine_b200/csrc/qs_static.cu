@@ -30,9 +30,8 @@
 namespace qs {
 
 template <typename T>
-cudaError_t launch_row_kernel(const T*, int, int, RowParams, RowWindow, unsigned long long*,
-                              RowResult*, int*, int*, int*, float*, int, ExpFix, RowScratch,
-                              cudaStream_t, long long* phase_cycles);
+cudaError_t launch_rows(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*, int*,
+                        int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t, long long* phase_cycles);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, float*, cudaStream_t);
 
@@ -47,6 +46,11 @@ struct StaticScratch {
     int slow_list[kStaticMaxBatch];
     int slow_count[4];
     unsigned long long rng[kStaticMaxBatch];  // greedy rows draw no uniform; never read
+    // the row kernel's per-row counters: each row's finishing CTA leaves them
+    // at zero, so they need clearing only when the array is first used on a
+    // device (or after a call that did not complete)
+    int done[kStaticMaxBatch];
+    unsigned long long gmax[kStaticMaxBatch];
 };
 
 static __device__ __align__(256) unsigned char g_static_scratch[sizeof(StaticScratch)];
@@ -120,6 +124,7 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
     if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "cudaGetDevice", cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return static_fail(QS_ERR_UNSUPPORTED, "device ordinal too large");
     void* ctx = current_context();
+    cudaStream_t st = (cudaStream_t)stream;
     StaticScratch* sc = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_static_mu);
@@ -128,12 +133,16 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
             e = cudaGetSymbolAddress(&p, g_static_scratch);
             if (e != cudaSuccess || !p)
                 return static_fail(QS_ERR_CUDA, "cudaGetSymbolAddress", cudaGetErrorString(e));
-            g_static_ptr[dev] = reinterpret_cast<StaticScratch*>(p);
+            StaticScratch* a = reinterpret_cast<StaticScratch*>(p);
+            // the row kernel's counters start at zero (its finishing CTAs
+            // leave them so after every call)
+            e = cudaMemsetAsync(a->done, 0, sizeof(a->done) + sizeof(a->gmax), st);
+            if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "clearing the counters", cudaGetErrorString(e));
+            g_static_ptr[dev] = a;
             g_static_ctx[dev] = current_context();  // the lookup made the context current
         }
         sc = g_static_ptr[dev];
     }
-    cudaStream_t st = (cudaStream_t)stream;
     const bool penalties = window > 0 && (repetition_penalty != 1.0f ||
                                           frequency_penalty != 0.0f || presence_penalty != 0.0f);
     RowWindow win{};
@@ -146,14 +155,16 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
     }
     const RowParams rp{0.0f, 1.0f, 0.0f, 0, 0u};  // temperature 0: the argmax branch
     const ExpFix none{nullptr, nullptr, nullptr, 0u};
+    RowScratch scr{};
+    scr.done = sc->done;
+    scr.gmax = sc->gmax;
     if (dtype == QS_F32)
-        e = launch_row_kernel<float>((const float*)d_logits, batch, vocab, rp, win, sc->rng, sc->res,
-                                     sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none,
-                                     RowScratch{}, st, nullptr);
+        e = launch_rows<float>((const float*)d_logits, batch, vocab, rp, win, sc->rng, sc->res,
+                               sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none, scr, st, nullptr);
     else
-        e = launch_row_kernel<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, rp, win,
-                                             sc->rng, sc->res, sc->slow_list, sc->slow_count,
-                                             nullptr, nullptr, 0, none, RowScratch{}, st, nullptr);
+        e = launch_rows<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, rp, win, sc->rng,
+                                       sc->res, sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none,
+                                       scr, st, nullptr);
     if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "row kernel", cudaGetErrorString(e));
     e = launch_emit(batch, vocab, 0, sc->res, d_tokens, nullptr, nullptr, nullptr, nullptr, nullptr,
                     nullptr, st);

@@ -273,6 +273,17 @@ class Sampler:
         check(_lib.lib.qs_profile_read(self._h, C.byref(p)))
         return {f: getattr(p, f) for f, _ in _lib.Profile._fields_}
 
+    def profile_phases(self, on: bool = True) -> None:
+        """Per-row clock64() phase stamps of the row kernel and the tie replay
+        (kernel tuning)."""
+        check(_lib.lib.qs_profile_phases(self._h, 1 if on else 0))
+
+    def profile_phases_read(self, which: int, n: int) -> np.ndarray:
+        out = np.zeros(n, dtype=np.int64)
+        check(_lib.lib.qs_profile_phases_read(self._h, int(which),
+                                              out.ctypes.data_as(C.POINTER(C.c_longlong)), int(n)))
+        return out
+
     def reset_history(self) -> None:
         check(_lib.lib.qs_reset_sampler_history(self._h))
 
