@@ -188,10 +188,11 @@ QS_API int qs_profile_enable(qs_sampler* s, int on);
 QS_API int qs_profile_reset(qs_sampler* s);
 QS_API int qs_profile_read(qs_sampler* s, qs_profile* out);
 
-/* Phase clocks for kernel tuning: with phases on, the row kernel records 12
- * clock64() stamps per row (which = 0) and the tie replay 16 per queued row in
- * queue order (which = 1) into device buffers that qs_profile_phases_read
- * copies out (n entries, synchronising the handle's device first). */
+/* Phase clocks for kernel tuning: with phases on, the row kernels record 12
+ * clock64() stamps per row (which = 0) and the tie replay 16 per queued
+ * row in queue order (which = 1), into device buffers that
+ * qs_profile_phases_read copies out (n entries, synchronising the handle's
+ * device first). */
 QS_API int qs_profile_phases(qs_sampler* s, int on);
 QS_API int qs_profile_phases_read(qs_sampler* s, int which, long long* host_out, int n);
 
@@ -282,6 +283,13 @@ QS_API int qs_lm_head_sample(qs_sampler* s, const void* d_hidden, const void* d_
                              void* stream, unsigned flags);
 QS_API int qs_lm_head_logits(qs_sampler* s, const void** d_logits);
 QS_API int qs_lm_head_status(qs_sampler* s, void* stream);
+
+/* Test hook: the time limit, in nanoseconds, of the lm_head kernel's pipeline
+ * waits for launches made after the call (0 restores the default, 2 s).  A
+ * limit of a few nanoseconds makes the waits run out, so that a test can see
+ * the kernel give up cleanly (error flag set, TMEM freed, the context still
+ * usable) without any fault.  Not for production use. */
+QS_API int qs_lm_head_set_wait_limit(unsigned long long ns);
 
 /* Message for the last error on the calling thread ("" if none). */
 QS_API const char* qs_last_error(void);

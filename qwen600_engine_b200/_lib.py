@@ -32,7 +32,7 @@ EXPORTS = (
     "qs_max_vocab", "qs_profile_enable", "qs_profile_reset", "qs_profile_read",
     "qs_profile_phases", "qs_profile_phases_read",
     "qs_argmax_rows_static", "qs_lm_head", "qs_lm_head_sample", "qs_lm_head_logits",
-    "qs_lm_head_status", "qs_lm_head_shard", "qs_ipc_handle_bytes", "qs_ipc_alloc", "qs_ipc_open",
+    "qs_lm_head_status", "qs_lm_head_set_wait_limit", "qs_lm_head_shard", "qs_ipc_handle_bytes", "qs_ipc_alloc", "qs_ipc_open",
     "qs_ipc_close", "qs_ipc_free",
 )
 
@@ -98,6 +98,7 @@ def _load() -> C.CDLL:
     lib.qs_lm_head_sample.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp, u32]
     lib.qs_lm_head_logits.argtypes = [vp, P(vp)]
     lib.qs_lm_head_status.argtypes = [vp, vp]
+    lib.qs_lm_head_set_wait_limit.argtypes = [C.c_ulonglong]
     lib.qs_lm_head_shard.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, P(vp), i32, i32, vp, vp]
     lib.qs_ipc_handle_bytes.argtypes = []
     lib.qs_ipc_alloc.argtypes = [C.c_size_t, P(vp), vp]

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libqwen600_sampler.so")
-SOURCES = ["qs_row.cu", "qs_ties.cu", "qs_sort.cu", "qs_api.cu", "qs_static.cu", "qs_lmhead.cu"]
+SOURCES = ["qs_row.cu", "qs_row_wide.cu", "qs_ties.cu", "qs_sort.cu", "qs_api.cu", "qs_static.cu", "qs_lmhead.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "--fmad=false", "-std=c++17", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-I", CSRC,
@@ -97,7 +97,33 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")
+    build_integration(verbose, force)
     return LIB
+
+
+INTEG = os.path.join(ROOT, "integration")
+DEMO_LIB = os.path.join(INTEG, "libqs_decode_demo.so")
+
+
+def build_integration(verbose: bool = False, force: bool = False) -> str:
+    """integration/libqs_decode_demo.so: a decode loop written against the
+    reference sampler's interface (integration/qs_sampler_compat.h), linked to
+    the sampler library."""
+    src = os.path.join(INTEG, "decode_demo.cu")
+    deps = [src, os.path.join(INTEG, "qs_sampler_compat.h"), os.path.join(ROOT, "include", "qwen600_sampler.h"),
+            LIB, __file__]
+    if not force and not _stale(DEMO_LIB, deps):
+        return DEMO_LIB
+    cmd = [nvcc()] + ARCH + ["-O2", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+                             "-Xcompiler", "-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-I", INTEG,
+                             src, "-o", DEMO_LIB, "-L", HERE, "-lqwen600_sampler",
+                             "-Xlinker", "-rpath,$ORIGIN/../qwen600_engine_b200"]
+    if verbose:
+        print(" ".join(cmd))
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"building the decode demo failed:\n{r.stderr}")
+    return DEMO_LIB
 
 
 if __name__ == "__main__":

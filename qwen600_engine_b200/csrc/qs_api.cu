@@ -1,7 +1,9 @@
 // C ABI of the B200 sampler (include/qwen600_sampler.h): handle lifetime,
 // parameter / RNG / history management and the launch sequence
-//   row_kernel (chunk scans; each row's last chunk finishes it) ->
-//   select_kernel (rows whose draw depends on the reference's tie order) -> emit_kernel
+//   row passes (batches of kWideMinRows rows and more: one CTA per row,
+//     qs_row_wide.cu; smaller ones: chunk scans, gathers and a finishing CTA
+//     per row, qs_row.cu) ->
+//   ties_kernel (rows whose draw depends on the reference's tie order) -> emit_kernel
 // on the caller's stream.  All device memory is allocated in
 // qs_build_sampler; the sampling entry points allocate nothing.
 #include <cuda_bf16.h>
@@ -21,16 +23,29 @@
 namespace qs {
 
 template <typename T>
-cudaError_t launch_rows(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*, int*,
-                        int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t,
-                        long long* phase_cycles = nullptr);
+cudaError_t launch_row_scan(const T*, int, int, RowParams, RowWindow, RowResult*, RowScratch, cudaStream_t);
+namespace wide {  // one CTA per row (qs_row_wide.cu)
+template <typename T>
+cudaError_t launch_row_stream(const T*, int, int, RowParams, RowWindow, RowResult*, RowScratch, cudaStream_t,
+                              long long* phase_cycles);
+template <typename T>
+cudaError_t launch_row_finish(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*,
+                              int*, int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t,
+                              long long* phase_cycles);
+}  // namespace wide
+// Batches of at least this many rows run one CTA per row (every SM holds
+// rows); smaller ones spread each row over chunks of CTAs.
+constexpr int kWideMinRows = 256;
+template <typename T>
+cudaError_t launch_row_finish(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*,
+                              int*, int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t,
+                              long long* phase_cycles);
 cudaError_t launch_write_penalized(float*, int, int, const int*, const int*, const float*, int,
                                    cudaStream_t);
 template <typename T>
-cudaError_t launch_select_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
-                                 const int*, const int*, RowResult*, RowScratch, int*, int*, int, int,
-                                 int*, float*, int, ExpFix, cudaStream_t, long long* phase_cycles,
-                                 long long* clusters_out);
+cudaError_t launch_ties_kernel(const T*, int, TieParams, const int*, const int*, const float*, int,
+                               const int*, const int*, RowResult*, unsigned long long*, int*, int,
+                               int*, float*, int, ExpFix, cudaStream_t, long long* phase_cycles);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, float*, cudaStream_t);
 template <typename T>
@@ -45,6 +60,7 @@ cudaError_t launch_lm_head(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bflo
                            int, int*, cudaStream_t);
 cudaError_t launch_rmsnorm(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int,
                            cudaStream_t);
+void lm_head_set_wait_ns(unsigned long long);
 cudaError_t launch_lm_head_shard(const __nv_bfloat16*, const __nv_bfloat16*, int, int, int, int, int*,
                                  const LhPeer&, cudaStream_t);
 
@@ -127,10 +143,16 @@ struct qs_sampler {
     ExpFix fix() const { return ExpFix{exp_off, exp_ent, exp_bloom, (uint32_t)QS_EXP_NB}; }
     // the row kernel's hand-over from a row's chunk scans to its finishing CTA
     float* rs_segm = nullptr;
-    int* rs_done = nullptr;                   // [B] chunks scanned
+    int* rs_done = nullptr;                   // [B] chunks scanned (greedy)
     unsigned long long* rs_gmax = nullptr;    // [B]
+    int2* rs_stash = nullptr;                 // [B, kStashCap]
+    int* rs_used = nullptr;                   // [B]
+    int* rs_chunk = nullptr;                  // [2, B, max chunks]: offsets, lengths
+    float* rs_chunk_lb = nullptr;             // [B, max chunks]
     RowScratch scratch() const {
-        return RowScratch{rs_segm, row_scratch_seg_stride(vocab), rs_done, rs_gmax};
+        const int mc = row_max_chunks(vocab);
+        return RowScratch{rs_segm, row_scratch_seg_stride(vocab), rs_done, rs_gmax, rs_stash, kStashCap,
+                          rs_used, rs_chunk, rs_chunk + (size_t)max_batch * mc, rs_chunk_lb, mc};
     }
     // launch accounting and optional per-kernel event timing
     bool profiling = false;
@@ -199,7 +221,7 @@ static void release(qs_sampler* s) {
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts, s->slot_counts,
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
                     s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm, s->rs_done,
-                    s->rs_gmax, s->st_hist, s->st_counts, s->st_count, s->st_rng, s->ph_row, s->ph_sel};
+                    s->rs_gmax, s->rs_stash, s->rs_used, s->rs_chunk, s->rs_chunk_lb, s->st_hist, s->st_counts, s->st_count, s->st_rng, s->ph_row, s->ph_sel};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
@@ -298,6 +320,10 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     ALLOC(s->rng, sizeof(unsigned long long) * B);
     ALLOC(s->rs_segm, sizeof(float) * B * (size_t)row_scratch_seg_stride(vocab));
     ALLOC(s->rs_done, sizeof(int) * B);
+    ALLOC(s->rs_stash, sizeof(int2) * B * (size_t)kStashCap);
+    ALLOC(s->rs_used, sizeof(int) * B);
+    ALLOC(s->rs_chunk, sizeof(int) * 2 * B * (size_t)row_max_chunks(vocab));
+    ALLOC(s->rs_chunk_lb, sizeof(float) * B * (size_t)row_max_chunks(vocab));
     ALLOC(s->rs_gmax, sizeof(unsigned long long) * B);
     ALLOC(s->d_in, sizeof(float) * B * V);
     ALLOC(s->st_hist, sizeof(int) * B * (size_t)s->ov_stride);
@@ -339,7 +365,10 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
                        cudaMemcpyHostToDevice);
     }
     if (e == cudaSuccess) e = cudaMemset(s->rs_done, 0, sizeof(int) * B);
+    if (e == cudaSuccess) e = cudaMemset(s->rs_used, 0, sizeof(int) * B);
     if (e == cudaSuccess) e = cudaMemset(s->rs_gmax, 0, sizeof(unsigned long long) * B);
+    // chunk records start empty (offset 0, length 0), never stale memory
+    if (e == cudaSuccess) e = cudaMemset(s->rs_chunk, 0, sizeof(int) * 2 * B * (size_t)row_max_chunks(vocab));
     if (e == cudaSuccess && W > 0) {
         e = cudaMemset(s->hcount, 0, sizeof(int) * B);
         if (e == cudaSuccess) e = cudaMemset(s->hpos, 0, sizeof(int) * B);
@@ -500,36 +529,60 @@ static int run(qs_sampler* s, const Call& c) {
     const int* ovn = penalties ? s->ov_n : nullptr;
     CK(cudaMemsetAsync(s->slow_count, 0, sizeof(int), c.stream));
     RowParams rp{p.temperature, p.topp, p.minp, p.top_k, c.flags};
+    const bool wide = B >= kWideMinRows;
     {
+        // the rows' streaming pass (wide batches), or their chunk scans and
+        // gathers
         KernelScope ks(s, 0, c.stream);
-        if (c.dtype == QS_F32)
-            CK(launch_rows<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res, s->slow_list,
-                                  s->slow_count, c.cand_index, c.cand_prob, c.cand_cap, s->fix(),
-                                  s->scratch(), c.stream, s->ph_row));
+        if (wide && c.dtype == QS_F32)
+            CK(wide::launch_row_stream<float>((const float*)c.logits, B, V, rp, win, s->res, s->scratch(),
+                                              c.stream, s->ph_row));
+        else if (wide)
+            CK(wide::launch_row_stream<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, s->res,
+                                                      s->scratch(), c.stream, s->ph_row));
+        else if (c.dtype == QS_F32)
+            CK(launch_row_scan<float>((const float*)c.logits, B, V, rp, win, s->res, s->scratch(), c.stream));
         else
-            CK(launch_rows<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng, s->res,
-                                          s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
-                                          c.cand_cap, s->fix(), s->scratch(), c.stream, s->ph_row));
+            CK(launch_row_scan<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, s->res,
+                                              s->scratch(), c.stream));
+    }
+    if (!greedy) {
+        KernelScope ks(s, 1, c.stream);
+        if (wide && c.dtype == QS_F32)
+            CK(wide::launch_row_finish<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res,
+                                              s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
+                                              c.cand_cap, s->fix(), s->scratch(), c.stream, s->ph_row));
+        else if (wide)
+            CK(wide::launch_row_finish<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng,
+                                                      s->res, s->slow_list, s->slow_count, c.cand_index,
+                                                      c.cand_prob, c.cand_cap, s->fix(), s->scratch(),
+                                                      c.stream, s->ph_row));
+        else if (c.dtype == QS_F32)
+            CK(launch_row_finish<float>((const float*)c.logits, B, V, rp, win, c.rng, s->res, s->slow_list,
+                                        s->slow_count, c.cand_index, c.cand_prob, c.cand_cap, s->fix(),
+                                        s->scratch(), c.stream, s->ph_row));
+        else
+            CK(launch_row_finish<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, c.rng, s->res,
+                                                s->slow_list, s->slow_count, c.cand_index, c.cand_prob,
+                                                c.cand_cap, s->fix(), s->scratch(), c.stream, s->ph_row));
     }
     if (!greedy && topk && !(c.flags & QS_FLAG_INDEX_TIES)) {
         // rows whose draw depends on the reference's tie arrangement: the
         // quick_select replay (one cluster per row; scratch slot per cluster)
         KernelScope ks(s, 2, c.stream);
         TieParams tp{p.temperature, p.topp, p.minp, p.top_k};
-        int* idx_scratch = reinterpret_cast<int*>(s->tie_scratch);
+        const int nct = B < s->tie_ctas ? B : s->tie_ctas;
+        s->prof.tie_clusters = nct;
         cudaError_t e;
         if (c.dtype == QS_F32)
-            e = launch_select_kernel<float>((const float*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val,
-                                            s->ov_stride, s->slow_list, s->slow_count, s->res, s->scratch(),
-                                            s->tie_pos, idx_scratch, B, s->tie_ctas, c.cand_index,
-                                            c.cand_prob, c.cand_cap, s->fix(), c.stream, s->ph_sel,
-                                            &s->prof.tie_clusters);
+            e = launch_ties_kernel<float>((const float*)c.logits, V, tp, ovn, s->ov_idx, s->ov_val, s->ov_stride,
+                                          s->slow_list, s->slow_count, s->res, s->tie_scratch, s->tie_pos, nct,
+                                          c.cand_index, c.cand_prob, c.cand_cap, s->fix(), c.stream, s->ph_sel);
         else
-            e = launch_select_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, V, tp, ovn, s->ov_idx,
-                                                    s->ov_val, s->ov_stride, s->slow_list, s->slow_count,
-                                                    s->res, s->scratch(), s->tie_pos, idx_scratch, B,
-                                                    s->tie_ctas, c.cand_index, c.cand_prob, c.cand_cap,
-                                                    s->fix(), c.stream, s->ph_sel, &s->prof.tie_clusters);
+            e = launch_ties_kernel<__nv_bfloat16>((const __nv_bfloat16*)c.logits, V, tp, ovn, s->ov_idx,
+                                                  s->ov_val, s->ov_stride, s->slow_list, s->slow_count, s->res,
+                                                  s->tie_scratch, s->tie_pos, nct, c.cand_index, c.cand_prob,
+                                                  c.cand_cap, s->fix(), c.stream, s->ph_sel);
         if (e == cudaErrorInvalidValue)
             return fail(QS_ERR_UNSUPPORTED, "tie replay: vocabulary %d with top_k %d exceeds shared memory", V, p.top_k);
         CK(e);
@@ -906,6 +959,12 @@ int qs_lm_head_status(qs_sampler* s, void* stream) {
         CK(cudaMemset(s->lh_err, 0, sizeof(int)));
         return fail(QS_ERR_CUDA, "lm_head kernel gave up waiting (a pipeline wait passed its time limit)");
     }
+    return QS_OK;
+}
+
+int qs_lm_head_set_wait_limit(unsigned long long ns) {
+    g_err.clear();
+    lm_head_set_wait_ns(ns);
     return QS_OK;
 }
 

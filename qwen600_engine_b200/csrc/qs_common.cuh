@@ -49,19 +49,26 @@ struct LhPeer {
 };
 
 struct RowScratch {
-    float* segm;               // [rows][seg_stride] segment maxima (chunk scans -> the row's finish;
-                               // the finish writes back the penalised maxima of window segments)
+    float* segm;               // [rows][seg_stride] penalised segment maxima (scan -> gather, finish)
     int seg_stride;
-    int* done;                 // [rows] chunks scanned; the last one finishes the row, then clears
-                               // done and gmax for the next call
-    unsigned long long* gmax;  // [rows] greedy rows: packed (order key, ~index) of the largest
-                               // logit outside the penalty window
+    int* done;                 // [rows] greedy: chunks scanned; the last one finishes the row and
+                               // clears done and gmax for the next call
+    unsigned long long* gmax;  // [rows] greedy: packed (order key, ~index) of the largest
+                               // penalised logit so far
+    int2* stash;               // [rows][stash_cap] (index, t bits): the rows' significant elements
+    int stash_cap;
+    int* stash_used;           // [rows] entries claimed (the finish clears it)
+    int* chunk_off;            // [rows][max_chunks] where each chunk's run starts (-1: none)
+    int* chunk_n;              // [rows][max_chunks] its length (-1: overflowed)
+    float* chunk_lb;           // [rows][max_chunks] the largest significance bound it used
+    int max_chunks;
 };
 // Segment maxima per row that fit either element type (fp32 segments are the
 // shorter: 128 elements).
 inline int row_scratch_seg_stride(int V) { return (V + 127) / 128; }
 constexpr int kRowChunkSegs = 64;  // segments per chunk scan (one CTA each)
 inline int row_chunks(int V, int seg) { return ((V + seg - 1) / seg + kRowChunkSegs - 1) / kRowChunkSegs; }
+inline int row_max_chunks(int V) { return row_chunks(V, 128); }  // the shorter (fp32) segments
 
 struct TieParams {
     float temperature, topp, minp;

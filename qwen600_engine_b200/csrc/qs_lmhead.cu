@@ -32,6 +32,7 @@
 #include <cub/block/block_reduce.cuh>
 
 #include "qs_common.cuh"
+#include "qs_pipe.cuh"
 
 namespace qs {
 
@@ -71,52 +72,7 @@ struct LhTile {
     }
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void mbar_init(unsigned long long* b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(unsigned long long* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Waits for the phase of `parity` to complete; false if the kernel is
-// aborting or `limit_ns` passed (then it raises the abort flag).
-__device__ bool mbar_wait(unsigned long long* b, uint32_t parity, volatile int* abort,
-                          unsigned long long limit_ns = kLhWaitNs) {
-    if (mbar_try(b, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (uint32_t it = 1;; it++) {
-        if (mbar_try(b, parity)) return true;
-        if ((it & 127u) == 0) {
-            if (*abort) return false;
-            if (global_ns() - t0 > limit_ns) {
-                *abort = 1;
-                return false;
-            }
-        }
-    }
-}
+constexpr unsigned long long kLhDrainNs = 100000000ull;  // 100 ms
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, unsigned long long* bar,
                                             int c0, int c1) {
     asm volatile(
@@ -166,7 +122,8 @@ template <int N>
 __global__ void __launch_bounds__(kLhThreads, 1)
 lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int tma_out, __nv_bfloat16* __restrict__ out, int B,
-               int V, int K, int ntiles, int* __restrict__ err, const __grid_constant__ LhPeer peer) {
+               int V, int K, int ntiles, int* __restrict__ err, const __grid_constant__ LhPeer peer,
+               unsigned long long wait_ns) {
     using Tl = LhTile<N>;
     constexpr uint32_t kLhStageB = Tl::kStageB;
     constexpr uint32_t kLhOutTile = Tl::kOutTile;
@@ -218,7 +175,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             bool stop = false;
             for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
                 for (int kb = 0; kb < nk; kb++) {
-                    if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort)) { stop = true; break; }
+                    if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort, wait_ns)) { stop = true; break; }
                     mbar_expect_tx(&sh->full[s], kLhStageA + kLhStageB);
                     tma_load_2d(sA + s * kLhStageA, &tmA, &sh->full[s], kb * kLhK, 0);
                     tma_load_2d(sB + s * kLhStageB, &tmB, &sh->full[s], kb * kLhK, tile * kLhN);
@@ -229,7 +186,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (*abort) {
                 // let the copies this thread issued land before the CTA leaves
                 for (int i = 0; i < kLhStages; i++)
-                    if (last_ph[i] >= 0) mbar_wait(&sh->full[i], (uint32_t)last_ph[i], abort, 100000000ull);
+                    if (last_ph[i] >= 0) mbar_wait(&sh->full[i], (uint32_t)last_ph[i], abort, kLhDrainNs, false);
             }
         }
     } else if (warp == 1) {
@@ -244,11 +201,11 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x, it++) {
                 const int b = it & 1;
                 const uint32_t use = (uint32_t)(it >> 1);
-                if (!mbar_wait(&sh->tempty[b], (use & 1u) ^ 1u, abort)) break;
+                if (!mbar_wait(&sh->tempty[b], (use & 1u) ^ 1u, abort, wait_ns)) break;
                 tc_fence_after();
                 const uint32_t dt = tbase + (uint32_t)b * kLhAccStride;
                 for (int kb = 0; kb < nk; kb++) {
-                    if (!mbar_wait(&sh->full[s], ph, abort)) { stop = true; break; }
+                    if (!mbar_wait(&sh->full[s], ph, abort, wait_ns)) { stop = true; break; }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + s * kLhStageA);
                     const uint32_t b0 = smem_u32(sB + s * kLhStageB);
@@ -263,9 +220,11 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 if (stop) break;
                 umma_commit(&sh->tfull[b]);
+                last_bar = &sh->tfull[b];
+                last_par = use & 1u;
             }
-            if (*abort && last_bar)  // the MMAs already issued finish before TMEM is freed
-                mbar_wait(last_bar, last_par, abort, 100000000ull);
+            if (*abort && last_bar)  // the MMAs and commits issued complete before TMEM is freed
+                mbar_wait(last_bar, last_par, abort, kLhDrainNs, false);
         }
     } else {
         // ---- epilogue: warps 2..5, each on its quarter of the TMEM lanes
@@ -286,7 +245,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, it++) {
             const int b = it & 1;
             const uint32_t use = (uint32_t)(it >> 1);
-            if (!mbar_wait(&sh->tfull[b], use & 1u, abort)) break;
+            if (!mbar_wait(&sh->tfull[b], use & 1u, abort, wait_ns)) break;
             tc_fence_after();
             const int n0 = tile * kLhN;
             if (tma_out && lane == 0)  // the previous tile's store has read the staging rows
@@ -400,6 +359,11 @@ rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __
 }
 
 // ------------------------------------------------------------- host side
+// The time limit of the kernel's pipeline waits; lm_head_set_wait_ns lets a
+// test make them run out (0 restores the default).
+static unsigned long long g_wait_ns = kLhWaitNs;
+void lm_head_set_wait_ns(unsigned long long ns) { g_wait_ns = ns ? ns : kLhWaitNs; }
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -450,7 +414,8 @@ static cudaError_t lm_head_go(const CUtensorMap& ma, const __nv_bfloat16* W, __n
     const size_t smem = LhTile<N>::smem();
     cudaError_t e = cudaFuncSetAttribute(lm_head_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    lm_head_kernel<N><<<grid, kLhThreads, smem, stream>>>(ma, mb, mc, tma_out, logits, B, V, K, ntiles, err, peer);
+    lm_head_kernel<N><<<grid, kLhThreads, smem, stream>>>(ma, mb, mc, tma_out, logits, B, V, K, ntiles, err, peer,
+                                                            g_wait_ns);
     return cudaGetLastError();
 }
 

@@ -266,6 +266,11 @@ __device__ __forceinline__ float vec_max<float>(const uint4& r) {
 }
 
 // ------------------------------------------------------------- block helpers
+// Barrier of the threads that run a row pass (the whole CTA); the block
+// helpers take it as a parameter.
+struct CtaSync {
+    __device__ __forceinline__ static void sync() { __syncthreads(); }
+};
 __device__ __forceinline__ float rblock_max(float v, float* red) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     v = warp_max(v);
@@ -284,6 +289,7 @@ __device__ __forceinline__ int rblock_min_int(int v, int* red) {
     const int r = lane < kRowWarps ? red[lane] : 0x7fffffff;
     return warp_min_int(r);
 }
+template <class Sync = CtaSync>
 __device__ __forceinline__ int rblock_excl_scan(int v, int* red, int* total) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     int x = v;
@@ -292,9 +298,9 @@ __device__ __forceinline__ int rblock_excl_scan(int v, int* red, int* total) {
         const int y = __shfl_up_sync(0xffffffffu, x, o);
         if (lane >= o) x += y;
     }
-    __syncthreads();
+    Sync::sync();
     if (lane == 31) red[w] = x;
-    __syncthreads();
+    Sync::sync();
     if (w == 0) {
         int s = lane < kRowWarps ? red[lane] : 0;
 #pragma unroll
@@ -304,7 +310,7 @@ __device__ __forceinline__ int rblock_excl_scan(int v, int* red, int* total) {
         }
         if (lane < kRowWarps) red[lane] = s;
     }
-    __syncthreads();
+    Sync::sync();
     const int before = (w == 0) ? 0 : red[w - 1];
     *total = red[kRowWarps - 1];
     return before + x - v;
@@ -1092,50 +1098,555 @@ __device__ __noinline__ void finish_by_segments(RowView<T> rv, int nseg, const f
     }
 }
 
-// ------------------------------------------------------------- the row kernel
-// One CTA per chunk of kRowChunkSegs segments of one row (grid: rows x
-// chunks).  Every CTA streams its chunk once from HBM (8 segments in flight
-// per warp) and leaves in global scratch the chunk's raw segment maxima or,
-// for greedy rows, the chunk's largest logit outside the penalty window with
-// its lowest index.  The last CTA of a row to finish (a ticket on the row's
-// counter) finishes the row: the penalty window (sampler.h:114-141), the
-// stash of the elements that may matter to the softmax sum (gathered from
-// the segments the chunks have just streamed, mostly still in L2), the
-// exact softmax denominator, the candidates, min-p / top-p and the draw.
-// Rows thus finish while other rows still stream, and a batch of a few rows
-// still spreads over the whole GPU.
+// ------------------------------------------------------------- row kernels
+// A call runs three launches over the rows:
+//
+//  scan    rows x chunks CTAs; every chunk of kRowChunkSegs segments is
+//          streamed once from HBM (8 segments in flight per warp).  The
+//          window's tokens are replayed per occurrence (sampler.h:114-141)
+//          and substituted exactly, so the chunk leaves the penalised maxima
+//          of its segments -- or, for greedy rows, its largest penalised
+//          logit with the lowest index; greedy rows are finished by their
+//          last chunk (a ticket on the row's counter).
+//  gather  rows x chunks CTAs; from the maxima of all earlier segments each
+//          chunk knows the exact significance threshold of its segments
+//          (an element below (maximum t of all earlier elements) - 17.5
+//          cannot change the reference's running fp32 sum), re-reads the
+//          segments that reach it and stashes their significant elements, in
+//          index order, in the row's stash.
+//  finish  one CTA per row: the stash in index order, the exact sequential
+//          softmax sum, the candidates, min-p / top-p and the draw.
+//
+// Chunks make every row's work spread over many CTAs, so small batches still
+// fill the GPU and large ones balance across SMs.
+
+
+// Penalty window of one row in shared memory, built by row_window_replay.
+struct WinSmem {
+    unsigned long long* pairs;  // [2 * npairs] (token, slot) keys, sorted
+    int* ofirst;                // [ovs] slot tokens, then each distinct token's first pair
+    float* pcnt;                // [ovs] token_counts of each slot
+    int* ovi;                   // [ovs] distinct window tokens, ascending
+    float* ovv;                 // [ovs] their penalised logits (tokens in [lo_idx, hi_idx) only)
+    float* rawslot;             // [ovs] raw logit of each slot's token (same range)
+    __host__ __device__ static size_t bytes(int window) {
+        const int ovs = window > 0 ? window : 1;
+        int np = 1;
+        while (np < ovs) np <<= 1;
+        return 16 * (size_t)np + 20 * (size_t)ovs;
+    }
+    __device__ WinSmem(unsigned char* base, int window) {
+        const int ovs = window > 0 ? window : 1;
+        int np = 1;
+        while (np < ovs) np <<= 1;
+        pairs = reinterpret_cast<unsigned long long*>(base);
+        ofirst = reinterpret_cast<int*>(pairs + 2 * np);
+        pcnt = reinterpret_cast<float*>(ofirst + ovs);
+        ovi = reinterpret_cast<int*>(pcnt + ovs);
+        ovv = reinterpret_cast<float*>(ovi + ovs);
+        rawslot = ovv + ovs;
+    }
+};
+
+// The row's window (sampler.h:114-141): slots sorted by (token, slot), the
+// distinct in-range tokens (ovi, ascending) and, for the tokens in
+// [lo_idx, hi_idx), their penalised logits (ovv), each replaying the token's
+// occurrences in slot order from its raw logit.  With write_tables every
+// token of the window is listed and the override tables are written (the
+// caller spans the whole row); without, only the tokens of [lo_idx, hi_idx)
+// are listed.  Returns the number of tokens listed (block-wide; every thread).
+template <typename T, class Sync = CtaSync>
+__device__ int row_window_replay(const T* __restrict__ Lrow, int V, int row, const RowWindow& win,
+                                 const WinSmem& w, int lo_idx, int hi_idx, bool write_tables, int* red_i,
+                                 int* sh_int) {
+    const int tid = threadIdx.x;
+    const bool pen_possible = win.hist && win.count && (win.rp != 1.0f || win.fp != 0.0f || win.pp != 0.0f);
+    if (tid == 0) {
+        int c = pen_possible ? win.count[row] : 0;
+        sh_int[0] = c < 0 ? 0 : (c > win.window ? win.window : c);
+        sh_int[1] = 0;
+    }
+    if (pen_possible)
+        for (int i = tid; i < win.window; i += kRowThreads) {
+            w.ofirst[i] = win.hist[(size_t)row * win.window + i];
+            w.pcnt[i] = win.slot_counts ? win.slot_counts[(size_t)row * win.window + i] : 0.0f;
+        }
+    Sync::sync();
+    const int cntw = sh_int[0];
+    if (cntw == 0) return 0;
+    int npow = 1;
+    while (npow < cntw) npow <<= 1;
+    unsigned long long* keys = w.pairs + npow;  // unsorted (token, slot) keys
+    for (int i = tid; i < npow; i += kRowThreads) {
+        const int t = i < cntw ? w.ofirst[i] : -1;
+        // without the tables only the tokens of [lo_idx, hi_idx) take part
+        const bool valid = t >= 0 && t < V && (write_tables || (t >= lo_idx && t < hi_idx));
+        keys[i] = valid ? (((unsigned long long)(unsigned)t << 32) | (unsigned)i) : ~0ull;
+        if (valid && t >= lo_idx && t < hi_idx) w.rawslot[i] = Elem<T>::widen(Lrow[t]);
+    }
+    Sync::sync();
+    if (npow <= 256) {
+        // rank sort (keys differ in the slot): one pass, one barrier
+        for (int i = tid; i < npow; i += kRowThreads) {
+            const unsigned long long x = keys[i];
+            int r = 0;
+            for (int j = 0; j < npow; j++) r += keys[j] < x || (keys[j] == x && j < i);
+            w.pairs[r] = x;
+        }
+        Sync::sync();
+    } else {
+        for (int i = tid; i < npow; i += kRowThreads) w.pairs[i] = keys[i];
+        Sync::sync();
+        for (int size = 2; size <= npow; size <<= 1) {  // ascending bitonic sort
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = tid; i < npow / 2; i += kRowThreads) {
+                    const int lo = 2 * stride * (i / stride) + (i % stride);
+                    const int hi = lo + stride;
+                    const bool up = ((lo & size) == 0);
+                    const unsigned long long x = w.pairs[lo], y = w.pairs[hi];
+                    if ((x > y) == up) { w.pairs[lo] = y; w.pairs[hi] = x; }
+                }
+                Sync::sync();
+            }
+        }
+    }
+    // distinct tokens: rank by an exclusive scan of "first of its token" flags
+    const int per = (npow + kRowThreads - 1) / kRowThreads;
+    const int c0 = min(tid * per, npow), c1 = min(c0 + per, npow);
+    int nd = 0, nvalid = 0;
+    for (int i = c0; i < c1; i++) {
+        const bool valid = w.pairs[i] != ~0ull;
+        nvalid += valid;
+        nd += valid && (i == 0 || (w.pairs[i] >> 32) != (w.pairs[i - 1] >> 32));
+    }
+    if (nvalid) atomicAdd(&sh_int[1], nvalid);
+    int tot;
+    int k = rblock_excl_scan<Sync>(nd, red_i, &tot);
+    for (int i = c0; i < c1; i++) {
+        if (w.pairs[i] != ~0ull && (i == 0 || (w.pairs[i] >> 32) != (w.pairs[i - 1] >> 32))) {
+            w.ovi[k] = (int)(w.pairs[i] >> 32);
+            w.ofirst[k] = i;
+            k++;
+        }
+    }
+    const int nov = tot;
+    Sync::sync();
+    const int nv = sh_int[1];
+    for (int j = tid; j < nov; j += kRowThreads) {
+        const int t = w.ovi[j];
+        if (t < lo_idx || t >= hi_idx) continue;
+        const int q1 = (j + 1 < nov) ? w.ofirst[j + 1] : nv;
+        float x = w.rawslot[(int)(w.pairs[w.ofirst[j]] & 0xFFFFFFFFull)];
+        for (int q = w.ofirst[j]; q < q1; q++) {
+            if (win.rp != 1.0f) x = (x > 0.0f) ? __fdiv_rn(x, win.rp) : __fmul_rn(x, win.rp);
+            if (win.fp != 0.0f)
+                x = __fsub_rn(x, __fmul_rn(win.fp, w.pcnt[(int)(w.pairs[q] & 0xFFFFFFFFull)]));
+            if (win.pp != 0.0f) x = __fsub_rn(x, win.pp);
+        }
+        w.ovv[j] = x;
+        if (write_tables && win.ov_idx) {
+            win.ov_idx[(size_t)row * win.ov_stride + j] = t;
+            win.ov_val[(size_t)row * win.ov_stride + j] = x;
+        }
+    }
+    Sync::sync();
+    return nov;
+}
+
+// First index j in [a, b) of the ascending ovi with ovi[j] >= x.
+__device__ __forceinline__ int lower_bound_int(const int* ovi, int a, int b, int x) {
+    while (a < b) {
+        const int m = (a + b) >> 1;
+        if (ovi[m] < x) a = m + 1; else b = m;
+    }
+    return a;
+}
+
+// Scan: penalised segment maxima (or, greedy, the chunk's argmax).
 template <typename T>
-__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
-row_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, RowWindow win,
-           unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
-           int* __restrict__ slow_list, int* __restrict__ slow_count,
-           int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
-           ExpFix fx, int ccap, int scap, RowScratch scr, long long* __restrict__ phase_cycles) {
+__global__ void __launch_bounds__(kRowThreads, kStreamMinBlocks)
+row_scan_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, RowWindow win,
+                RowResult* __restrict__ res, RowScratch scr) {
     constexpr int EPL = Elem<T>::kPerLane;
     constexpr int SEG = 32 * EPL;
-    constexpr int US = kRowChunkSegs / kRowWarps;  // segments in flight per warp in the scan
-    constexpr int U = 2;  // gathered segments in flight per warp in the finish (more held
-                          // more registers than the 80 the kernel is sized for)
+    constexpr int US = kRowChunkSegs / kRowWarps;  // segments in flight per warp
     const int row = blockIdx.x / nchunk;
     const int chunk = blockIdx.x - row * nchunk;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nseg = (V + SEG - 1) / SEG;
+    const bool greedy = prm.temperature < 1e-6f;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const WinSmem w(smem, win.window);
+    __shared__ int red_i[32];
+    __shared__ int sh_int[4];
+    __shared__ unsigned long long s_best;
+
+    RowView<T> rv;
+    rv.L = logits + (size_t)row * V;
+    rv.V = V;
+    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
+    const int g0 = chunk * kRowChunkSegs;
+    const int lo_idx = g0 * SEG;
+    const int hi_idx = min(V, (g0 + kRowChunkSegs) * SEG);
+    uint4 rs[US];
+#pragma unroll
+    for (int u = 0; u < US; u++) {
+        const int g = g0 + warp + u * kRowWarps;
+        rs[u] = (g < nseg && rv.full(g, lane)) ? rv.raw(g, lane) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (tid == 0) s_best = 0ull;
+    // the window while the chunk's loads are in flight
+    // (the first chunk replays the whole window and writes the override
+    // tables; the others replay only their own tokens)
+    const bool tables = chunk == 0;
+    const int nov = row_window_replay<T>(rv.L, V, row, win, w, tables ? 0 : lo_idx, tables ? V : hi_idx,
+                                         tables, red_i, sh_int);
+    if (tables && tid == 0 && win.ov_n) win.ov_n[row] = nov;
+    const int j0 = lower_bound_int(w.ovi, 0, nov, lo_idx);
+    const int j1 = lower_bound_int(w.ovi, j0, nov, hi_idx);
+
+#pragma unroll
+    for (int u = 0; u < US; u++) {
+        const int g = g0 + warp + u * kRowWarps;
+        if (g >= nseg) continue;  // warp-uniform
+        const int base = g * SEG;
+        const int jg = lower_bound_int(w.ovi, j0, j1, base);
+        const bool wseg = jg < j1 && w.ovi[jg] < base + SEG;
+        float v[EPL];
+        bool have = false;
+        if (!greedy && !wseg && rv.aligned && base + SEG <= V) {
+            const float m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(vec_max<T>(rs[u]))));
+            if (lane == 0) scr.segm[(size_t)row * scr.seg_stride + g] = m;
+        } else {
+            rv.widen_raw(g, lane, rv.full(g, lane), rs[u], v);
+            have = true;
+        }
+        if (!have) continue;
+        const int lb = base + lane * EPL;
+        if (wseg) {
+            // the window tokens' penalised logits in place of their raw ones
+            int j = lower_bound_int(w.ovi, jg, j1, lb);
+#pragma unroll
+            for (int e = 0; e < EPL; e++)
+                if (j < j1 && w.ovi[j] == lb + e) { v[e] = w.ovv[j]; j++; }
+        }
+        if (!greedy) {
+            float m = v[0];
+#pragma unroll
+            for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
+            const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
+            if (lane == 0) scr.segm[(size_t)row * scr.seg_stride + g] = fkey_inv(km);
+        } else {
+            // the largest penalised logit, lowest index first (sample_argmax's
+            // strict '>', sampler.h:100-111: NaN never taken, -0 == +0)
+            float bm = 0.0f;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const float x = v[e];
+                if (lb + e < V && x == x && (bi == 0x7fffffff || x > bm)) { bm = x; bi = lb + e; }
+            }
+            unsigned long long key = 0ull;
+            if (bi != 0x7fffffff)
+                key = ((unsigned long long)fkey(bm == 0.0f ? 0.0f : bm) << 32) | (unsigned long long)(~(uint32_t)bi);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, o);
+                key = y > key ? y : key;
+            }
+            if (lane == 0 && key) atomicMax(&s_best, key);
+        }
+    }
+    if (!greedy) return;
+    if (chunk == 0 && tid == 0) {
+        // sample_argmax starts from logits[0] with a strict '>': a NaN there
+        // (after the penalties) wins, so the row's token is 0
+        const float l0 = (nov > 0 && w.ovi[0] == 0) ? w.ovv[0] : Elem<T>::widen(rv.L[0]);
+        if (!(l0 == l0)) atomicMax(&s_best, ~0ull);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        if (s_best) atomicMax(scr.gmax + row, s_best);
+        __threadfence();
+        sh_int[2] = atomicAdd(scr.done + row, 1) == nchunk - 1;
+    }
+    __syncthreads();
+    if (!sh_int[2] || tid != 0) return;
+    __threadfence();
+    const unsigned long long best = __ldcg(scr.gmax + row);
+    scr.gmax[row] = 0ull;  // the row's counters start at zero for the next call
+    scr.done[row] = 0;
+    RowResult out;
+    const int token = best ? (int)(~(uint32_t)(best & 0xFFFFFFFFull)) : 0;
+    out.token = (token >= 0 && token < V) ? token : 0;
+    out.greedy = 1; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
+    out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0;
+    out.max_logit = best ? fkey_inv((uint32_t)(best >> 32)) : 0.0f;
+    out.sum = 0.f; out.r = 0.f; out.renorm_sum = 0.f; out.inv_temp = 0.f; out.sum_inv = 0.f;
+    out.status = 0; out.pad_ = 0;
+    res[row] = out;
+}
+
+constexpr int kGatherStage = 2048;  // stashed elements one chunk can hold
+
+// Gather: the significant elements of one chunk, in index order, appended to
+// the row's stash (the chunk's offset and count recorded; a count of -1 marks
+// an overflow, which sends the row to the dense method).
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads, 4)
+row_gather_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, RowWindow win,
+                  RowScratch scr) {
+    constexpr int EPL = Elem<T>::kPerLane;
+    constexpr int SEG = 32 * EPL;
+    constexpr int U = 2;  // hot segments in flight per warp
+    const int row = blockIdx.x / nchunk;
+    const int chunk = blockIdx.x - row * nchunk;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nseg = (V + SEG - 1) / SEG;
+    const int g0 = chunk * kRowChunkSegs;
+    const int g1 = min(nseg, g0 + kRowChunkSegs);
+    const int ng = g1 - g0;
+    const float inv = __fdiv_rn(1.0f, prm.temperature);
+    const float* segm_row = scr.segm + (size_t)row * scr.seg_stride;
+    __shared__ float pre[kRowChunkSegs];       // exclusive prefix maximum of t per chunk segment
+    __shared__ int hot[kRowChunkSegs];
+    __shared__ int sgb[kRowChunkSegs], sgc[kRowChunkSegs];  // each segment's run in the staging
+    __shared__ unsigned char segov[kRowChunkSegs];
+    __shared__ float red_f[32];
+    __shared__ int sh_int[6];
+    __shared__ uint32_t sh_lb;
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* st_t = reinterpret_cast<float*>(smem);             // [kGatherStage]
+    int* st_i = reinterpret_cast<int*>(st_t + kGatherStage);  // [kGatherStage]
+    int* ovi = st_i + kGatherStage;                           // [window] the chunk's window tokens
+    float* ovv = reinterpret_cast<float*>(ovi + (win.window > 0 ? win.window : 1));
+
+    // the maximum t over the segments before the chunk (all of a thread's
+    // loads in flight together), the chunk's own maxima
+    float m = -INFINITY;
+    for (int g0b = tid; g0b < g0; g0b += 4 * kRowThreads) {
+        float x[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int g = g0b + u * kRowThreads;
+            x[u] = g < g0 ? __ldcg(segm_row + g) : -INFINITY;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) m = fmaxf(m, __fmul_rn(x[u], inv));
+    }
+    m = warp_max(m);
+    if (lane == 0) red_f[warp] = m;
+    if (tid < kRowChunkSegs) { segov[tid] = 0; sgc[tid] = 0; }
+    if (tid == 0) { sh_int[0] = 0; sh_int[1] = 0; sh_int[2] = 0; sh_lb = fkey(-INFINITY); }
+    // the chunk's window tokens (penalised), from the override tables
+    const int nov_row = (win.ov_n && win.ov_idx) ? win.ov_n[row] : 0;
+    const int lo_idx = g0 * SEG, hi_idx = g1 * SEG;
+    __syncthreads();
+    for (int j = tid; j < nov_row; j += kRowThreads) {
+        // the row's tables are ascending: the chunk's tokens are one run
+        const int q = win.ov_idx[(size_t)row * win.ov_stride + j];
+        const bool in = q >= lo_idx && q < hi_idx;
+        if (in && (j == 0 || win.ov_idx[(size_t)row * win.ov_stride + j - 1] < lo_idx)) sh_int[4] = j;
+        if (in) atomicAdd(&sh_int[2], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float x = lane < kRowWarps ? red_f[lane] : -INFINITY;
+        x = warp_max(x);
+        // exclusive prefix maximum over the chunk's segments (two per lane)
+        float a[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = 2 * lane + h;
+            a[h] = j < ng ? __fmul_rn(__ldcg(segm_row + g0 + j), inv) : -INFINITY;
+        }
+        float y = fmaxf(a[0], a[1]);
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float z = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) y = fmaxf(y, z);
+        }
+        float before = __shfl_up_sync(0xffffffffu, y, 1);
+        if (lane == 0) before = -INFINITY;
+        before = fmaxf(before, x);
+        pre[2 * lane] = before;
+        pre[2 * lane + 1] = fmaxf(before, a[0]);
+        // hot segments: their maximum reaches their threshold (the row's first
+        // segment always: each element against the elements before it)
+        int nh = 0;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = 2 * lane + h;
+            const float pj = h == 0 ? before : fmaxf(before, a[0]);
+            const bool ht = j < ng && (g0 + j == 0 || a[h] >= __fsub_rn(pj, kSigGap));
+            const unsigned b = __ballot_sync(0xffffffffu, ht);
+            if (ht) hot[nh + __popc(b & ((1u << lane) - 1u))] = j;
+            nh += __popc(b);
+        }
+        if (lane == 0) sh_int[3] = nh;
+    }
+    // the chunk's window tokens into shared memory (a contiguous run of the
+    // ascending tables)
+    const int nw = sh_int[2];
+    if (nw > 0) {
+        const int a = sh_int[4];
+        for (int j = tid; j < nw; j += kRowThreads) {
+            const int q = win.ov_idx[(size_t)row * win.ov_stride + a + j];
+            ovi[j] = q;
+            ovv[j] = win.ov_val[(size_t)row * win.ov_stride + a + j];
+            segov[q / SEG - g0] = 1;
+        }
+    }
+    __syncthreads();
+    const int nh = sh_int[3];
+    RowView<T> rv;
+    rv.L = logits + (size_t)row * V;
+    rv.V = V;
+    rv.aligned = (((size_t)V * sizeof(T)) % 16 == 0) && ((((uintptr_t)logits) & 15) == 0);
+    rv.segov = segov - g0;  // indexed by row segment
+    rv.ovi = ovi;
+    rv.ovv = ovv;
+    rv.nov = nw;
+    float lbmax = ng > 0 ? pre[ng - 1] : -INFINITY;  // the largest threshold used (+ 17.5)
+    uint4 r[U];
+    for (int h0 = warp; h0 < nh; h0 += U * kRowWarps) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int h = h0 + u * kRowWarps;
+            r[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (h < nh && rv.full(g0 + hot[h], lane)) r[u] = rv.raw(g0 + hot[h], lane);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int h = h0 + u * kRowWarps;
+            if (h >= nh) continue;
+            const int j = hot[h];
+            const int g = g0 + j;
+            float v[EPL];
+            rv.widen(g, lane, rv.full(g, lane), r[u], v);
+            float the[EPL];  // each element's threshold
+            const float th = __fsub_rn(pre[j], kSigGap);
+#pragma unroll
+            for (int e = 0; e < EPL; e++) { v[e] = __fmul_rn(v[e], inv); the[e] = th; }
+            if (g == 0) {
+                // the row's first segment: each element against the running
+                // maximum of the elements before it
+                float run = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) { the[e] = run; run = fmaxf(run, v[e]); }
+                float x = run;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x = fmaxf(x, y);
+                }
+                float before = __shfl_up_sync(0xffffffffu, x, 1);
+                if (lane == 0) before = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) the[e] = fmaxf(before, the[e]);
+                lbmax = fmaxf(lbmax, __shfl_sync(0xffffffffu, the[EPL - 1], 31));
+#pragma unroll
+                for (int e = 0; e < EPL; e++) the[e] = __fsub_rn(the[e], kSigGap);
+            }
+            unsigned keep = 0;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const bool kk = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
+                keep |= (kk ? 1u : 0u) << e;
+            }
+            const unsigned lt = (1u << lane) - 1u;
+            int before = 0, tot = 0;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const unsigned be = __ballot_sync(0xffffffffu, (keep >> e) & 1u);
+                before += __popc(be & lt);
+                tot += __popc(be);
+            }
+            if (tot == 0) continue;
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&sh_int[0], tot);
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (base + tot <= kGatherStage) {
+                if (lane == 0) { sgb[j] = base; sgc[j] = tot; }
+                int pos = base + before;
+#pragma unroll
+                for (int e = 0; e < EPL; e++)
+                    if ((keep >> e) & 1u) { st_t[pos] = v[e]; st_i[pos] = g * SEG + lane * EPL + e; pos++; }
+            } else if (lane == 0) {
+                sh_int[1] = 1;  // the staging overflowed
+            }
+        }
+    }
+    if (lane == 0) atomicMax(&sh_lb, fkey(lbmax));
+    __syncthreads();
+    // the chunk's largest bound, and its entries appended in segment (index)
+    // order to the row's stash
+    const int n = sh_int[0];
+    const size_t slot = (size_t)row * scr.max_chunks + chunk;
+    if (tid == 0) {
+        int off = -1;
+        if (!sh_int[1] && n > 0) {
+            off = atomicAdd(scr.stash_used + row, n);
+            if (off + n > scr.stash_cap) off = -1;
+        }
+        scr.chunk_off[slot] = off;
+        scr.chunk_n[slot] = (sh_int[1] || (n > 0 && off < 0)) ? -1 : n;
+        scr.chunk_lb[slot] = fkey_inv(sh_lb);
+        sh_int[5] = off;
+    }
+    __syncthreads();
+    const int off = sh_int[5];
+    if (off < 0 || n == 0) return;
+    // segment runs in order: an exclusive scan of the 64 run lengths
+    if (warp == 0) {
+        int c0 = sgc[2 * lane], c1 = sgc[2 * lane + 1];
+        int x = c0 + c1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        const int ex = x - c0 - c1;
+        hot[2 * lane] = ex;            // hot[] now holds each segment's output offset
+        hot[2 * lane + 1] = ex + c0;
+    }
+    __syncthreads();
+    int2* dst = scr.stash + (size_t)row * scr.stash_cap + off;
+    for (int j = warp; j < ng; j += kRowWarps) {
+        const int c = sgc[j];
+        for (int i = lane; i < c; i += 32) {
+            const int src = sgb[j] + i;
+            dst[hot[j] + i] = make_int2(st_i[src], __float_as_int(st_t[src]));
+        }
+    }
+}
+
+// Finish (non-greedy rows): the exact softmax denominator, the candidates,
+// min-p / top-p and the draw, from the penalised segment maxima, override
+// tables and stash the scan and gather left in `scr`; rows it cannot settle
+// go to the exact passes.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks)
+row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow win,
+                  unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
+                  int* __restrict__ slow_list, int* __restrict__ slow_count,
+                  int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
+                  ExpFix fx, int ccap, int scap, RowScratch scr, int nchunk,
+                  long long* __restrict__ phase_cycles) {
+    constexpr int EPL = Elem<T>::kPerLane;
+    constexpr int SEG = 32 * EPL;
+    const int row = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const RowSmem L(V, SEG, win.window, ccap, scap);
     const int nseg = L.nseg;
-    const bool greedy = prm.temperature < 1e-6f;
-    const float inv = greedy ? 1.0f : __fdiv_rn(1.0f, prm.temperature);
 
-    // ---- shared memory carve-up (the finish's layout; the scan uses little)
+    // ---- shared memory carve-up
     extern __shared__ __align__(16) unsigned char smem[];
     float* segm = (float*)(smem + L.segm);            // segment maxima (l, then t)
     uint32_t* segk = (uint32_t*)(smem + L.segk);      // order keys of segm (t)
     unsigned char* segov = smem + L.segov;
     int* ovi = (int*)(smem + L.ovi);
     float* ovv = (float*)(smem + L.ovv);
-    int* ofirst = (int*)(smem + L.ofirst);
-    unsigned long long* pairs = (unsigned long long*)(smem + L.pairs);
-    float* pcnt = (float*)(smem + L.pcnt);
-    float* rawv = (float*)(smem + L.rawv);            // window tokens' raw logits
-    int* rech = (int*)(smem + L.rech);                // segments whose maximum is recomputed
     unsigned char* region = smem + L.region;          // stash, or the dense method's tables
     float* st_t = (float*)region;
     int* st_i = (int*)(region + 4 * (size_t)scap);
@@ -1147,14 +1658,30 @@ row_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, RowWi
                    (int*)(smem + L.so), (unsigned long long*)(smem + L.ck),
                    (uint32_t*)(smem + L.rhist), ccap};
     __shared__ RowShared sh;
-    __shared__ uint32_t cwin[kRowChunkSegs / 32];  // chunk segments holding a window token
-    __shared__ unsigned long long cbest;         // greedy: packed (key, ~index) of the chunk's maximum
-    __shared__ int cnw, clast;
     const RowOut ro{res, slow_list, slow_count, cand_index_out, cand_prob_out, cand_cap, row};
 
     long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
     auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
+    stamp(10);
+    const float inv = __fdiv_rn(1.0f, prm.temperature);
 
+    // ---- what the scan left: penalised segment maxima; the window's
+    // overrides from the tables it wrote
+    const int nov = (win.ov_n && win.ov_idx) ? win.ov_n[row] : 0;
+    for (int g = tid; g < nseg; g += kRowThreads) {
+        segm[g] = scr.segm[(size_t)row * scr.seg_stride + g];
+        segov[g] = 0;
+        scnt[g] = 0;
+    }
+    if (tid == 0) { sh.nst = 0; sh.ovf = 0; sh.nhot = 0; sh.maxlb = fkey(-INFINITY); }
+    __syncthreads();
+    for (int j = tid; j < nov; j += kRowThreads) {
+        const int q = win.ov_idx[(size_t)row * win.ov_stride + j];
+        ovi[j] = q;
+        ovv[j] = win.ov_val[(size_t)row * win.ov_stride + j];
+        segov[q / SEG] = 1;
+    }
+    __syncthreads();
     RowView<T> rv;
     rv.L = logits + (size_t)row * V;
     rv.V = V;
@@ -1162,427 +1689,64 @@ row_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, RowWi
     rv.segov = segov;
     rv.ovi = ovi;
     rv.ovv = ovv;
-    rv.nov = 0;
-
-    // ---- the chunk scan: every vector of the chunk in flight at once
-    const int g0 = chunk * kRowChunkSegs;
-    uint4 rs[US];
-#pragma unroll
-    for (int u = 0; u < US; u++) {
-        const int g = g0 + warp + u * kRowWarps;
-        rs[u] = (g < nseg && rv.full(g, lane)) ? rv.raw(g, lane) : make_uint4(0u, 0u, 0u, 0u);
-    }
-    // the window's tokens in this chunk, read while the chunk streams
-    int* ctok = ofirst;  // greedy: this chunk's window tokens (room for the whole window)
-    if (tid < kRowChunkSegs / 32) cwin[tid] = 0u;
-    if (tid == 0) { cnw = 0; cbest = 0ull; }
-    __syncthreads();
-    const bool pen_possible = win.hist && win.count && (win.rp != 1.0f || win.fp != 0.0f || win.pp != 0.0f);
-    if (pen_possible) {
-        int cntw = win.count[row];
-        cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
-        for (int i = tid; i < cntw; i += kRowThreads) {
-            const int t = win.hist[(size_t)row * win.window + i];
-            if (t >= 0 && t < V) {
-                const int j = t / SEG - g0;
-                if (j >= 0 && j < kRowChunkSegs) {
-                    atomicOr(&cwin[j >> 5], 1u << (j & 31));
-                    if (greedy) ctok[atomicAdd(&cnw, 1)] = t;
-                }
-            }
-        }
-    }
-    __syncthreads();
-    if (greedy) {
-        // the largest logit of each segment outside the window, lowest index
-        // first (sample_argmax's strict '>', sampler.h:100-111; NaN never
-        // taken; -0 and +0 compare equal)
-        const int nw = cnw;
-#pragma unroll
-        for (int u = 0; u < US; u++) {
-            const int g = g0 + warp + u * kRowWarps;
-            if (g >= nseg) continue;  // warp-uniform
-            const int j = g - g0;
-            const bool wseg = (cwin[j >> 5] >> (j & 31)) & 1u;
-            float v[EPL];
-            rv.widen_raw(g, lane, rv.full(g, lane), rs[u], v);
-            float bm = 0.0f;
-            int bi = 0x7fffffff;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) {
-                const int idx = g * SEG + lane * EPL + e;
-                const float x = v[e];
-                bool ok = idx < V && x == x;
-                if (ok && wseg)
-                    for (int k = 0; k < nw; k++) ok = ok && ctok[k] != idx;
-                if (ok && (bi == 0x7fffffff || x > bm)) { bm = x; bi = idx; }
-            }
-            unsigned long long key = 0ull;
-            if (bi != 0x7fffffff)
-                key = ((unsigned long long)fkey(bm == 0.0f ? 0.0f : bm) << 32) | (unsigned long long)(~(uint32_t)bi);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, o);
-                key = y > key ? y : key;
-            }
-            if (lane == 0 && key) atomicMax(&cbest, key);
-        }
-    } else {
-#pragma unroll
-        for (int u = 0; u < US; u++) {
-            const int g = g0 + warp + u * kRowWarps;
-            if (g >= nseg) continue;  // warp-uniform
-            float m;
-            if (rv.aligned && (g + 1) * SEG <= V) {
-                m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(vec_max<T>(rs[u]))));
-            } else {
-                float v[EPL];
-                rv.widen_raw(g, lane, rv.full(g, lane), rs[u], v);
-                float lm2 = v[0];
-#pragma unroll
-                for (int e = 1; e < EPL; e++) lm2 = fmaxf(lm2, v[e]);
-                m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(lm2)));
-            }
-            if (lane == 0) scr.segm[(size_t)row * scr.seg_stride + g] = m;
-        }
-        if (lane == 0) __threadfence();  // the segment maxima before the row's ticket
-    }
-    // ---- the last chunk of the row to finish finishes the row
-    __syncthreads();
-    if (tid == 0) {
-        if (greedy && cbest) atomicMax(scr.gmax + row, cbest);
-        __threadfence();
-        clast = atomicAdd(scr.done + row, 1) == nchunk - 1;
-    }
-    __syncthreads();
-    if (!clast) return;
-    __threadfence();
-    stamp(0);
-    if (tid == 0) {
-        if (greedy) cbest = __ldcg(scr.gmax + row);
-        // clear the row's counters for the next call (no other CTA of this
-        // call touches them again)
-        scr.done[row] = 0;
-        scr.gmax[row] = 0ull;
-        sh.nst = 0; sh.ovf = 0; sh.nhot = 0; sh.maxlb = fkey(-INFINITY);
-        sh.misc[6] = 0; sh.misc[7] = 0;
-        int c5 = pen_possible ? win.count[row] : 0;
-        sh.misc[5] = c5 < 0 ? 0 : (c5 > win.window ? win.window : c5);
-    }
-    // the window's slots and their counts
-    if (pen_possible) {
-        for (int i = tid; i < win.window; i += kRowThreads) {
-            ofirst[i] = win.hist[(size_t)row * win.window + i];
-            pcnt[i] = win.slot_counts ? win.slot_counts[(size_t)row * win.window + i] : 0.0f;
-        }
-    }
-    for (int g = tid; g < nseg; g += kRowThreads) {
-        segov[g] = 0;
-        scnt[g] = 0;
-        if (!greedy) segm[g] = __ldcg(scr.segm + (size_t)row * scr.seg_stride + g);
-    }
-    __syncthreads();
-    // ---- the row's penalty window (sampler.h:114-141): slots sorted by
-    // (token, slot), distinct tokens and the slot range of each
-    int cntw = pen_possible ? sh.misc[5] : 0;  // (clamped again: the slot count is the caller's)
-    cntw = cntw < 0 ? 0 : (cntw > win.window ? win.window : cntw);
-    const bool pen_on = cntw > 0;
-    int nov = 0;
-    if (pen_on) {
-        int npow = 1;
-        while (npow < cntw) npow <<= 1;
-        unsigned long long* keys = pairs + npow;  // unsorted (token, slot) keys
-        float* rawslot = reinterpret_cast<float*>(rech);  // raw logit of each slot's token
-        const T* Lrow = logits + (size_t)row * V;
-        float raw0 = 0.0f;  // this thread's first slot: its load overlaps the sort
-        bool has0 = false;
-        for (int i = tid; i < npow; i += kRowThreads) {
-            const int t = i < cntw ? ofirst[i] : -1;
-            const bool valid = t >= 0 && t < V;
-            keys[i] = valid ? (((unsigned long long)(unsigned)t << 32) | (unsigned)i) : ~0ull;
-            if (i < cntw && !win.slot_counts) pcnt[i] = 0.0f;
-            if (valid) {
-                const float raw = Elem<T>::widen(Lrow[t]);
-                if (i == tid) { raw0 = raw; has0 = true; }
-                else rawslot[i] = raw;
-            }
-        }
-        __syncthreads();
-        if (npow <= 256) {
-            // rank sort (keys differ in the slot): one pass, one barrier
-            for (int i = tid; i < npow; i += kRowThreads) {
-                const unsigned long long x = keys[i];
-                int r = 0;
-                for (int j = 0; j < npow; j++) r += keys[j] < x || (keys[j] == x && j < i);
-                pairs[r] = x;
-            }
-            __syncthreads();
-        } else {
-            for (int i = tid; i < npow; i += kRowThreads) pairs[i] = keys[i];
-            __syncthreads();
-            for (int size = 2; size <= npow; size <<= 1) {  // ascending bitonic sort
-                for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                    for (int i = tid; i < npow / 2; i += kRowThreads) {
-                        const int lo = 2 * stride * (i / stride) + (i % stride);
-                        const int hi = lo + stride;
-                        const bool up = ((lo & size) == 0);
-                        const unsigned long long x = pairs[lo], y = pairs[hi];
-                        if ((x > y) == up) { pairs[lo] = y; pairs[hi] = x; }
-                    }
-                    __syncthreads();
-                }
-            }
-        }
-        if (has0) rawslot[tid] = raw0;
-        // distinct tokens: rank by an exclusive scan of "first of its token" flags
-        const int per = (npow + kRowThreads - 1) / kRowThreads;
-        const int c0 = tid * per, c1 = min(c0 + per, npow);
-        int nd = 0, nvalid = 0;
-        for (int i = c0; i < c1; i++) {
-            const bool valid = pairs[i] != ~0ull;
-            nvalid += valid;
-            nd += valid && (i == 0 || (pairs[i] >> 32) != (pairs[i - 1] >> 32));
-        }
-        if (nvalid) atomicAdd(&sh.misc[7], nvalid);
-        int tot;
-        int k = rblock_excl_scan(nd, sh.red_i, &tot);
-        for (int i = c0; i < c1; i++) {
-            if (pairs[i] != ~0ull && (i == 0 || (pairs[i] >> 32) != (pairs[i - 1] >> 32))) {
-                ovi[k] = (int)(pairs[i] >> 32);
-                ofirst[k] = i;
-                k++;
-            }
-        }
-        nov = tot;
-        __syncthreads();
-        const int nv = sh.misc[7];
-        // each window token's penalised value from its raw logit (that of its
-        // first slot), replaying its occurrences in slot order
-        for (int j = tid; j < nov; j += kRowThreads) {
-            const int t = ovi[j];
-            const int q1 = (j + 1 < nov) ? ofirst[j + 1] : nv;
-            const float raw = rawslot[(int)(pairs[ofirst[j]] & 0xFFFFFFFFull)];
-            float x = raw;
-            for (int q = ofirst[j]; q < q1; q++) {
-                if (win.rp != 1.0f) x = (x > 0.0f) ? __fdiv_rn(x, win.rp) : __fmul_rn(x, win.rp);
-                if (win.fp != 0.0f)
-                    x = __fsub_rn(x, __fmul_rn(win.fp, pcnt[(int)(pairs[q] & 0xFFFFFFFFull)]));
-                if (win.pp != 0.0f) x = __fsub_rn(x, win.pp);
-            }
-            ovv[j] = x;
-            rawv[j] = raw;
-            segov[t / SEG] = 1;
-            if (win.ov_idx) {
-                win.ov_idx[(size_t)row * win.ov_stride + j] = t;
-                win.ov_val[(size_t)row * win.ov_stride + j] = x;
-            }
-        }
-        __syncthreads();
-        // Fold, per segment holding window tokens (its first token's thread).
-        // When no token's raw logit equals the segment's raw maximum, the
-        // other elements hold that maximum, so the maximum of the penalised
-        // segment is the fmaxf of it and the penalised tokens.  Otherwise, or
-        // where a NaN or a zero is involved (fmaxf and the order keys may
-        // pick differently there), the segment is recomputed below with the
-        // penalised values substituted, as the streaming pass would have.
-        for (int j = tid; j < nov && !greedy; j += kRowThreads) {
-            const int g = ovi[j] / SEG;
-            if (j > 0 && ovi[j - 1] / SEG == g) continue;
-            const float sraw = segm[g];
-            float m = sraw;
-            bool redo = !(sraw == sraw) || sraw == 0.0f;
-            for (int k = j; k < nov && ovi[k] / SEG == g; k++) {
-                const float pv = ovv[k];
-                redo = redo || rawv[k] == sraw || !(pv == pv) || pv == 0.0f;
-                m = fmaxf(m, pv);
-            }
-            if (redo) rech[atomicAdd(&sh.misc[6], 1)] = g;
-            else segm[g] = m;
-        }
-        __syncthreads();
-    }
-    if (tid == 0 && win.ov_n) win.ov_n[row] = nov;
     rv.nov = nov;
-    for (int i = warp; i < sh.misc[6] && !greedy; i += kRowWarps) {
-        const int g = rech[i];
-        float v[EPL];
-        rv.load(g, lane, v);
-        float m = v[0];
-#pragma unroll
-        for (int e = 1; e < EPL; e++) m = fmaxf(m, v[e]);
-        const uint32_t km = __reduce_max_sync(0xffffffffu, fkey(m));
-        if (lane == 0) segm[g] = fkey_inv(km);
-    }
-    __syncthreads();
-    stamp(1);
-    // the penalised maxima of the window's segments back to the scratch (the
-    // tie pass bounds the top k by the segment maxima)
-    if (!greedy)
-        for (int j = tid; j < nov; j += kRowThreads) {
-            const int g = ovi[j] / SEG;
-            if (j == 0 || ovi[j - 1] / SEG != g) scr.segm[(size_t)row * scr.seg_stride + g] = segm[g];
-        }
-    if (greedy) {
-        // the window tokens' penalised values against the largest logit
-        // outside the window (lowest index first among equal values)
-        for (int j = tid; j < nov; j += kRowThreads) {
-            const float x = ovv[j];
-            if (x == x) {
-                const unsigned long long key =
-                    ((unsigned long long)fkey(x == 0.0f ? 0.0f : x) << 32) | (unsigned long long)(~(uint32_t)ovi[j]);
-                atomicMax(&cbest, key);
-            }
-        }
-        __syncthreads();
-        if (tid == 0) {
-            const unsigned long long best = cbest;
-            int token = best ? (int)(~(uint32_t)(best & 0xFFFFFFFFull)) : 0;
-            // sample_argmax starts from logits[0] and compares with a strict
-            // '>': when the penalised logits[0] is NaN no element compares
-            // above it and the reference returns 0
-            const float l0 = (nov > 0 && ovi[0] == 0) ? ovv[0] : Elem<T>::widen(rv.L[0]);
-            if (!(l0 == l0)) token = 0;
-            RowResult out;
-            out.token = (token >= 0 && token < V) ? token : 0;
-            out.greedy = 1; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
-            out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0;
-            out.max_logit = best ? fkey_inv((uint32_t)(best >> 32)) : l0;
-            out.sum = 0.f; out.r = 0.f; out.renorm_sum = 0.f; out.inv_temp = 0.f; out.sum_inv = 0.f;
-            out.status = 0; out.pad_ = 0;
-            res[row] = out;
-        }
-        return;
-    }
-
     float lm = -INFINITY;
     for (int g = tid; g < nseg; g += kRowThreads) lm = fmaxf(lm, segm[g]);
     const float maxl = rblock_max(lm, sh.red_f);
 
-    // ---- the stash: every element that may be significant for the softmax
-    // sum, t >= pre - 17.5 where pre is the maximum t before it (the exact
-    // maximum of the segments before its segment; in the first segment, of
-    // the elements before it).  A segment is gathered when its maximum
-    // reaches its threshold; the gathered segments are re-read U at a time
-    // per warp, all U loads in flight together.
-    float* pre = reinterpret_cast<float*>(segk);  // exclusive prefix maximum of t per segment (segk is set later)
-    __syncthreads();                              // red_f is free again
-    {
-        // block-wide exclusive max-scan over the segments, per thread a run
-        const int per = (nseg + kRowThreads - 1) / kRowThreads;
-        const int c0 = min(tid * per, nseg), c1 = min(c0 + per, nseg);
-        float m = -INFINITY;
-        for (int g = c0; g < c1; g++) m = fmaxf(m, __fmul_rn(segm[g], inv));
-        float x = m;
+    // ---- the stash the gather left: the chunks' runs (each in index order)
+    // concatenated in chunk order; an overflow anywhere sends the row to the
+    // dense method
+    __shared__ int ch_dst[32], ch_off[32], ch_n[32];
+    if (warp == 0) {
+        const size_t slot = (size_t)row * scr.max_chunks + lane;
+        const bool inr = lane < nchunk;
+        const int n = inr ? __ldcg(scr.chunk_n + slot) : 0;
+        const int off = inr ? __ldcg(scr.chunk_off + slot) : 0;
+        const float lb = inr ? __ldcg(scr.chunk_lb + slot) : -INFINITY;
+        // a record that does not lie inside the row's stash counts as an overflow
+        const bool bad = inr && (n < 0 || off < 0 || n > scap || off > scr.stash_cap - n);
+        int x = bad ? 0 : n;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= o) x = fmaxf(x, y);
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
         }
-        if (lane == 31) sh.red_f[warp] = x;
-        __syncthreads();
-        float wpre = -INFINITY;
-        for (int w = 0; w < warp; w++) wpre = fmaxf(wpre, sh.red_f[w]);
-        float ex = __shfl_up_sync(0xffffffffu, x, 1);
-        if (lane == 0) ex = -INFINITY;
-        float run = fmaxf(wpre, ex);
-        for (int g = c0; g < c1; g++) {
-            pre[g] = run;
-            run = fmaxf(run, __fmul_rn(segm[g], inv));
+        const int tot = __shfl_sync(0xffffffffu, x, 31);
+        const bool ovf = __any_sync(0xffffffffu, bad) || tot > scap;
+        ch_dst[lane] = x - (bad ? 0 : n);
+        ch_off[lane] = off;
+        ch_n[lane] = bad ? 0 : n;
+        const float lbm = warp_max(lb);
+        if (lane == 0) {
+            sh.ovf = ovf ? 1 : 0;
+            sh.nst = ovf ? 0 : tot;
+            sh.maxlb = fkey(lbm);
+            scr.stash_used[row] = 0;  // the row's counter starts at zero for the next call
         }
-        __syncthreads();
     }
-    {
-        // the largest threshold used (+ 17.5): the stash holds every t >= lbmax - 17.5
-        float lbmax = nseg > 1 ? pre[nseg - 1] : -INFINITY;
-        int* hot = reinterpret_cast<int*>(smem + L.hotl);  // the segments to gather, in any order
-        uint4 r[U];
-        for (int g = tid; g < nseg; g += kRowThreads)
-            if (g == 0 || __fmul_rn(segm[g], inv) >= __fsub_rn(pre[g], kSigGap)) hot[atomicAdd(&sh.nhot, 1)] = g;
-        __syncthreads();
-        const int nhot = sh.nhot;
-        // every gathered segment's lines requested into L2 at once (4 per segment),
-        // so the gather's batches after the first find them there
-        for (int q = tid; q < 4 * nhot; q += kRowThreads)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(rv.L + (size_t)hot[q >> 2] * SEG) + (q & 3) * 128));
-        for (int h0 = warp; h0 < nhot; h0 += U * kRowWarps) {
-    #pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int h = h0 + u * kRowWarps;
-                r[u] = make_uint4(0u, 0u, 0u, 0u);
-                if (h < nhot && rv.full(hot[h], lane)) r[u] = rv.raw(hot[h], lane);
-            }
-    #pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int h = h0 + u * kRowWarps;
-                if (h >= nhot) continue;
-                const int g = hot[h];
-                if (*(volatile int*)&sh.ovf) continue;  // the dense method takes over; stop stashing
-                float v[EPL];
-                rv.widen(g, lane, rv.full(g, lane), r[u], v);
-                float the[EPL];  // each element's threshold
-                const float th = __fsub_rn(pre[g], kSigGap);
-    #pragma unroll
-                for (int e = 0; e < EPL; e++) { v[e] = __fmul_rn(v[e], inv); the[e] = th; }
-                if (g == 0) {
-                    // the first segment: each element against the running maximum
-                    // of the elements before it
-                    float run = -INFINITY;
-    #pragma unroll
-                    for (int e = 0; e < EPL; e++) { the[e] = run; run = fmaxf(run, v[e]); }
-                    float x = run;
-    #pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const float y = __shfl_up_sync(0xffffffffu, x, o);
-                        if (lane >= o) x = fmaxf(x, y);
-                    }
-                    float before = __shfl_up_sync(0xffffffffu, x, 1);
-                    if (lane == 0) before = -INFINITY;
-    #pragma unroll
-                    for (int e = 0; e < EPL; e++) the[e] = fmaxf(before, the[e]);
-                    lbmax = fmaxf(lbmax, __shfl_sync(0xffffffffu, the[EPL - 1], 31));
-    #pragma unroll
-                    for (int e = 0; e < EPL; e++) the[e] = __fsub_rn(the[e], kSigGap);
-                }
-                unsigned keep = 0;
-    #pragma unroll
-                for (int e = 0; e < EPL; e++) {
-                    const bool kk = (g * SEG + lane * EPL + e < V) && v[e] >= the[e];
-                    keep |= (kk ? 1u : 0u) << e;
-                }
-                // the kept elements' places in index order: one ballot per slot of
-                // the lanes' vectors (independent, no scan chain)
-                const unsigned lt = (1u << lane) - 1u;
-                int before = 0, tot = 0;
-    #pragma unroll
-                for (int e = 0; e < EPL; e++) {
-                    const unsigned be = __ballot_sync(0xffffffffu, (keep >> e) & 1u);
-                    before += __popc(be & lt);
-                    tot += __popc(be);
-                }
-                if (tot == 0) continue;
-                int base = 0;
-                if (lane == 0) base = atomicAdd(&sh.nst, tot);
-                base = __shfl_sync(0xffffffffu, base, 0);
-                if (base + tot <= scap) {
-                    if (lane == 0) { sstart[g] = base; scnt[g] = tot; }
-                    int pos = base + before;
-    #pragma unroll
-                    for (int e = 0; e < EPL; e++) {
-                        if ((keep >> e) & 1u) {
-                            st_t[pos] = v[e];
-                            st_i[pos] = g * SEG + lane * EPL + e;
-                            pos++;
-                        }
-                    }
-                } else if (lane == 0) {
-                    sh.ovf = 1;
-                }
+    __syncthreads();
+    if (!sh.ovf) {
+        const int2* stash = scr.stash + (size_t)row * scr.stash_cap;
+        for (int c = 0; c < nchunk; c++) {
+            const int n = ch_n[c], off = ch_off[c], dst = ch_dst[c];
+            for (int i = tid; i < n; i += kRowThreads) {
+                const int2 e = __ldcg(stash + off + i);
+                st_i[dst + i] = e.x;
+                st_t[dst + i] = __int_as_float(e.y);
             }
         }
-        if (lane == 0) atomicMax(&sh.maxlb, fkey(lbmax));
         __syncthreads();
+        const int nst = sh.nst;
+        for (int i = tid; i < nst; i += kRowThreads) {
+            const int g = st_i[i] / SEG;
+            if (i == 0 || st_i[i - 1] / SEG != g) sstart[g] = i;
+            atomicAdd(&scnt[g], 1);
+        }
     }
+    __syncthreads();
     stamp(2);
+
     RowResult out;
     out.token = 0; out.greedy = 0; out.n_topk = 0; out.n_minp = 0; out.n_final = 0;
     out.draw_pos = 0; out.exact_ties = 0; out.sum_fallback = 0; out.max_logit = maxl;
@@ -1799,42 +1963,69 @@ int row_kernel_ccap(int top_k, int V) {
     return c;
 }
 
-// The row kernel over `B` rows: rows x chunks CTAs.  `scr` holds per row
-// row_scratch_seg_stride(V) segment maxima and the two counters (zero before
-// the first call; each row's finishing CTA clears them again).  Greedy calls
-// use only the counters.
 template <typename T>
-cudaError_t launch_rows(const T* logits, int B, int V, RowParams prm, RowWindow win,
-                        unsigned long long* rng, RowResult* res, int* slow_list, int* slow_count,
-                        int* cand_index, float* cand_prob, int cand_cap, ExpFix fx, RowScratch scr,
-                        cudaStream_t stream, long long* phase_cycles) {
+cudaError_t launch_row_scan(const T* logits, int B, int V, RowParams prm, RowWindow win, RowResult* res,
+                            RowScratch scr, cudaStream_t stream) {
     if (B <= 0) return cudaSuccess;
-    const int ccap = row_kernel_ccap(prm.top_k, V);
     if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
     const bool greedy = prm.temperature < 1e-6f;
     if (!scr.done || !scr.gmax) return cudaErrorInvalidValue;
-    if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V)))
-        return cudaErrorInvalidValue;
     constexpr int SEG = 32 * (16 / (int)sizeof(T));
-    const RowSmem L(V, SEG, win.window, ccap, kStashCap);
-    cudaError_t err = cudaFuncSetAttribute(row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)L.total);
-    if (err != cudaSuccess) return err;
     const int nchunk = row_chunks(V, SEG);
+    if (!greedy && (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V) || !scr.stash ||
+                    !scr.stash_used || !scr.chunk_n || !scr.chunk_off || !scr.chunk_lb ||
+                    scr.max_chunks < nchunk))
+        return cudaErrorInvalidValue;
     const long long grid = (long long)B * nchunk;
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-    row_kernel<T><<<(unsigned)grid, kRowThreads, L.total, stream>>>(
-        logits, V, nchunk, prm, win, rng, res, slow_list, slow_count, cand_index, cand_prob, cand_cap,
-        fx, ccap, kStashCap, scr, phase_cycles);
+    const size_t wsm = WinSmem::bytes(win.window);
+    cudaError_t err = cudaFuncSetAttribute(row_scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)wsm);
+    if (err != cudaSuccess) return err;
+    row_scan_kernel<T><<<(unsigned)grid, kRowThreads, wsm, stream>>>(logits, V, nchunk, prm, win, res, scr);
+    err = cudaGetLastError();
+    if (err != cudaSuccess || greedy) return err;
+    const size_t gsm = 8 * (size_t)kGatherStage + 8 * (size_t)(win.window > 0 ? win.window : 1);
+    err = cudaFuncSetAttribute(row_gather_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    if (err != cudaSuccess) return err;
+    row_gather_kernel<T><<<(unsigned)grid, kRowThreads, gsm, stream>>>(logits, V, nchunk, prm, win, scr);
     return cudaGetLastError();
 }
 
-template cudaError_t launch_rows<float>(const float*, int, int, RowParams, RowWindow, unsigned long long*,
-                                        RowResult*, int*, int*, int*, float*, int, ExpFix, RowScratch,
-                                        cudaStream_t, long long*);
-template cudaError_t launch_rows<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
-                                                unsigned long long*, RowResult*, int*, int*, int*, float*,
-                                                int, ExpFix, RowScratch, cudaStream_t, long long*);
+// Finish (non-greedy calls).
+template <typename T>
+cudaError_t launch_row_finish(const T* logits, int B, int V, RowParams prm, RowWindow win,
+                              unsigned long long* rng, RowResult* res, int* slow_list, int* slow_count,
+                              int* cand_index, float* cand_prob, int cand_cap, ExpFix fx, RowScratch scr,
+                              cudaStream_t stream, long long* phase_cycles) {
+    if (B <= 0 || prm.temperature < 1e-6f) return cudaSuccess;  // greedy rows: finished by the scan
+    const int ccap = row_kernel_ccap(prm.top_k, V);
+    if (!win.hist || !win.count) { win.hist = nullptr; win.count = nullptr; win.window = 0; }
+    constexpr int SEG = 32 * (16 / (int)sizeof(T));
+    const int nchunk = row_chunks(V, SEG);
+    if (!scr.segm || scr.seg_stride < row_scratch_seg_stride(V) || scr.max_chunks < nchunk || nchunk > 32)
+        return cudaErrorInvalidValue;
+    const RowSmem L(V, SEG, win.window, ccap, kStashCap);
+    cudaError_t err = cudaFuncSetAttribute(row_finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)L.total);
+    if (err != cudaSuccess) return err;
+    row_finish_kernel<T><<<B, kRowThreads, L.total, stream>>>(logits, V, prm, win, rng, res, slow_list,
+                                                              slow_count, cand_index, cand_prob, cand_cap,
+                                                              fx, ccap, kStashCap, scr, nchunk, phase_cycles);
+    return cudaGetLastError();
+}
+
+template cudaError_t launch_row_scan<float>(const float*, int, int, RowParams, RowWindow, RowResult*,
+                                            RowScratch, cudaStream_t);
+template cudaError_t launch_row_scan<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
+                                                    RowResult*, RowScratch, cudaStream_t);
+template cudaError_t launch_row_finish<float>(const float*, int, int, RowParams, RowWindow,
+                                              unsigned long long*, RowResult*, int*, int*, int*, float*,
+                                              int, ExpFix, RowScratch, cudaStream_t, long long*);
+template cudaError_t launch_row_finish<__nv_bfloat16>(const __nv_bfloat16*, int, int, RowParams, RowWindow,
+                                                      unsigned long long*, RowResult*, int*, int*, int*,
+                                                      float*, int, ExpFix, RowScratch, cudaStream_t,
+                                                      long long*);
 
 // QS_FLAG_WRITE_PENALIZED: the reference's in-place penalty update of fp32
 // logits (sampler.h:114-141), written after every pass has read the raw row.

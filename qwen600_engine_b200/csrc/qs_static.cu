@@ -30,8 +30,7 @@
 namespace qs {
 
 template <typename T>
-cudaError_t launch_rows(const T*, int, int, RowParams, RowWindow, unsigned long long*, RowResult*, int*,
-                        int*, int*, float*, int, ExpFix, RowScratch, cudaStream_t, long long* phase_cycles);
+cudaError_t launch_row_scan(const T*, int, int, RowParams, RowWindow, RowResult*, RowScratch, cudaStream_t);
 cudaError_t launch_emit(int, int, int, const RowResult*, int*, qs_row_debug*, int*, int*, int*,
                         float*, float*, cudaStream_t);
 
@@ -159,12 +158,10 @@ QS_API int qs_argmax_rows_static(const void* d_logits, qs_dtype dtype, int batch
     scr.done = sc->done;
     scr.gmax = sc->gmax;
     if (dtype == QS_F32)
-        e = launch_rows<float>((const float*)d_logits, batch, vocab, rp, win, sc->rng, sc->res,
-                               sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none, scr, st, nullptr);
+        e = launch_row_scan<float>((const float*)d_logits, batch, vocab, rp, win, sc->res, scr, st);
     else
-        e = launch_rows<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, rp, win, sc->rng,
-                                       sc->res, sc->slow_list, sc->slow_count, nullptr, nullptr, 0, none,
-                                       scr, st, nullptr);
+        e = launch_row_scan<__nv_bfloat16>((const __nv_bfloat16*)d_logits, batch, vocab, rp, win, sc->res,
+                                           scr, st);
     if (e != cudaSuccess) return static_fail(QS_ERR_CUDA, "row kernel", cudaGetErrorString(e));
     e = launch_emit(batch, vocab, 0, sc->res, d_tokens, nullptr, nullptr, nullptr, nullptr, nullptr,
                     nullptr, st);

@@ -131,3 +131,34 @@ def test_lm_head_argument_errors():
     w = torch.zeros((64, 100), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(SamplerError):
         lm_head(h, w)   # hidden_dim not a multiple of 64
+
+
+def test_lm_head_gives_up_cleanly_when_its_waits_run_out():
+    """A wait limit of a few nanoseconds (the test hook) makes the pipeline
+    waits run out: the kernel raises its error flag, lets the copies and MMAs
+    it issued complete, frees its TMEM and returns.  The error is reported,
+    the context stays usable, and the next launch with the default limit
+    computes the right logits."""
+    torch = _torch()
+    from qwen600_engine_b200 import _lib
+    from qwen600_engine_b200.sampler import SamplerError, lm_head
+    h, w, nw = _inputs(torch, 128, 1024, W.VOCAB, seed=77)
+    normed_ok, logits_ok = lm_head(h, w, nw)
+    torch.cuda.synchronize()
+    gave_up = False
+    _lib.check(_lib.lib.qs_lm_head_set_wait_limit(1))
+    try:
+        for _ in range(3):
+            try:
+                lm_head(h, w, nw)
+            except SamplerError as e:
+                assert "gave up" in str(e)
+                gave_up = True
+                break
+    finally:
+        _lib.check(_lib.lib.qs_lm_head_set_wait_limit(0))
+    torch.cuda.synchronize()
+    assert gave_up, "no wait ran out under a 1 ns limit"
+    normed, logits = lm_head(h, w, nw)
+    torch.cuda.synchronize()
+    assert torch.equal(normed, normed_ok) and torch.equal(logits, logits_ok)

@@ -164,7 +164,25 @@ CASES = {
     # benchmark's batch 1024 top-k (bf16), where the tie pass queues ~4% of rows
     "nucleus_f32_64_full": lambda: W.nucleus_f32(B=64),
     "topk_bf16_1024_full": lambda: W.topk_bf16(B=1024),
+    # batches of 256 rows and more take the persistent streaming kernel
+    # (bf16 above; fp32 here, with Zipf windows and frequency / presence
+    # penalties)
+    "nucleus_f32_320_streamed": lambda: W.nucleus_f32(B=320, seed=31),
+    "greedy_f32_300_streamed": lambda: _greedy_f32(300),
 }
+
+
+def _greedy_f32(B):
+    """Greedy fp32 rows with penalties: the streaming kernel's argmax path
+    with window substitutions, exact duplicate maxima and a NaN at index 0."""
+    wl = W.nucleus_f32(B=B, seed=37)
+    wl.params = W.SamplingParams(0.0, 1.0, 0.0, 0, 1.3, 0.4, 0.25)
+    x = wl.logits
+    for r in range(0, B, 5):
+        m = int(np.argmax(x[r]))
+        x[r, (m + 777) % x.shape[1]] = x[r, m]
+    x[7, 0] = np.float32("nan")
+    return wl
 
 
 @pytest.mark.parametrize("name", list(CASES))
