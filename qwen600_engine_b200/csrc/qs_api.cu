@@ -149,10 +149,13 @@ struct qs_sampler {
     int* rs_used = nullptr;                   // [B]
     int* rs_chunk = nullptr;                  // [2, B, max chunks]: offsets, lengths
     float* rs_chunk_lb = nullptr;             // [B, max chunks]
+    float* rs_fb = nullptr;                   // [min(B, kWideMinRows), kFbCap, 256]
+    int fb_rows = 0;
     RowScratch scratch() const {
         const int mc = row_max_chunks(vocab);
         return RowScratch{rs_segm, row_scratch_seg_stride(vocab), rs_done, rs_gmax, rs_stash, kStashCap,
-                          rs_used, rs_chunk, rs_chunk + (size_t)max_batch * mc, rs_chunk_lb, mc};
+                          rs_used, rs_chunk, rs_chunk + (size_t)max_batch * mc, rs_chunk_lb, mc, rs_fb,
+                          fb_rows};
     }
     // launch accounting and optional per-kernel event timing
     bool profiling = false;
@@ -221,7 +224,7 @@ static void release(qs_sampler* s) {
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts, s->slot_counts,
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
                     s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm, s->rs_done,
-                    s->rs_gmax, s->rs_stash, s->rs_used, s->rs_chunk, s->rs_chunk_lb, s->st_hist, s->st_counts, s->st_count, s->st_rng, s->ph_row, s->ph_sel};
+                    s->rs_gmax, s->rs_stash, s->rs_used, s->rs_chunk, s->rs_chunk_lb, s->rs_fb, s->st_hist, s->st_counts, s->st_count, s->st_rng, s->ph_row, s->ph_sel};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& t : s->pending) { cudaEventDestroy(t.a); cudaEventDestroy(t.b); }
@@ -324,6 +327,8 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     ALLOC(s->rs_used, sizeof(int) * B);
     ALLOC(s->rs_chunk, sizeof(int) * 2 * B * (size_t)row_max_chunks(vocab));
     ALLOC(s->rs_chunk_lb, sizeof(float) * B * (size_t)row_max_chunks(vocab));
+    s->fb_rows = (int)(B < (size_t)kWideMinRows ? B : (size_t)kWideMinRows);  // the chunked finish's rows
+    ALLOC(s->rs_fb, sizeof(float) * 256 * kFbCap * (size_t)s->fb_rows);
     ALLOC(s->rs_gmax, sizeof(unsigned long long) * B);
     ALLOC(s->d_in, sizeof(float) * B * V);
     ALLOC(s->st_hist, sizeof(int) * B * (size_t)s->ov_stride);

@@ -62,7 +62,12 @@ struct RowScratch {
     int* chunk_n;              // [rows][max_chunks] its length (-1: overflowed)
     float* chunk_lb;           // [rows][max_chunks] the largest significance bound it used
     int max_chunks;
+    // dense rows: the exact terms of the hot segments whose running-sum binade
+    // cannot be predicted, formed in parallel before the sequential walk
+    float* fb_terms;           // [fb_rows][kFbCap][256]
+    int fb_rows;               // rows it has room for (0: none; the walk forms them itself)
 };
+constexpr int kFbCap = 64;      // segments per row with precomputed exact terms
 // Segment maxima per row that fit either element type (fp32 segments are the
 // shorter: 128 elements).
 inline int row_scratch_seg_stride(int V) { return (V + 127) / 128; }

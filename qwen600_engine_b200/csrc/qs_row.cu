@@ -45,6 +45,8 @@
 // (qs_exp.cuh).  In the dense method, where a value only feeds a rounding
 // decision, CUDA's expf decides unless a 4-ulp change of the value could
 // change that decision, in which case the exact value is formed.
+#include <cooperative_groups.h>
+
 #include "qs_common.cuh"
 
 namespace qs {
@@ -559,9 +561,20 @@ struct RowShared {
 // sum in sh->sum.  segm holds the segment maxima of t.
 template <typename T>
 __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* segm, float inv, float M,
-                                       unsigned char* region, float* wbuf, RowShared* sh, ExpFix fx) {
+                                       unsigned char* region, float* wbuf, RowShared* sh, ExpFix fx,
+                                       long long* ph, int crank, int csize, float* fb) {
     constexpr int EPL = RowView<T>::EPL;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // the per-segment loops are shared by the csize CTAs of a cluster: warp
+    // gw of nw takes every nw-th hot segment and writes its result into every
+    // CTA's table (approximate sums) or the first CTA's (transfer functions)
+    namespace cg = cooperative_groups;
+    const int gw = crank * kRowWarps + warp, nw = csize * kRowWarps;
+    auto cluster_sync = [&]() {
+        if (csize > 1) cg::this_cluster().sync();
+        else __syncthreads();
+    };
+    cluster_sync();  // every CTA of the cluster runs before any writes another's tables
     int* hot = (int*)region;                          // hot segment ids, in order
     float* hthr = (float*)(region + 4 * (size_t)nseg);
     float* hA = (float*)(region + 8 * (size_t)nseg);
@@ -611,21 +624,22 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
         if (tid == 0) sh->nhot = tot;
     }
     __syncthreads();
+    if (ph && threadIdx.x == 0) ph[0] = clock64();
     const int nhot = sh->nhot;
     // approximate sums of hot segments (binade prediction only, so CUDA's
     // fast exponential is good enough here)
-    for (int h0 = warp; h0 < nhot; h0 += kRowWarps * 4) {
+    for (int h0 = gw; h0 < nhot; h0 += nw * 4) {
         uint4 r[4];
         bool f[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-            const int h = h0 + u * kRowWarps;
+            const int h = h0 + u * nw;
             f[u] = (h < nhot) && rv.full(hot[h], lane);
             if (f[u]) r[u] = rv.raw(hot[h], lane);
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-            const int h = h0 + u * kRowWarps;
+            const int h = h0 + u * nw;
             if (h < nhot) {
                 float v[EPL];
                 rv.widen(hot[h], lane, f[u], r[u], v);
@@ -637,11 +651,15 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                     if (t >= thr) s += __expf(t - M);
                 }
                 s = warp_sum(s);
-                if (lane == 0) hA[h] = s;
+                if (lane == 0) {
+                    if (csize == 1) hA[h] = s;
+                    else
+                        for (int q = 0; q < csize; q++) cg::this_cluster().map_shared_rank(hA, q)[h] = s;
+                }
             }
         }
     }
-    __syncthreads();
+    cluster_sync();
     {
         const int per = (nhot + kRowThreads - 1) / kRowThreads;
         const int c0 = tid * per, c1 = min(c0 + per, nhot);
@@ -679,21 +697,56 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
             hE[h] = E;
             run += (double)hA[h];
         }
+        if (fb) {
+            // slots for the exact terms of the segments whose binade the
+            // prediction leaves open (the approximate sums are not read again)
+            int nu = 0;
+            for (int h = c0; h < c1; h++) nu += hE[h] == INT_MIN;
+            int totu;
+            int su = rblock_excl_scan(nu, sh->red_i, &totu);
+            int* hslot = reinterpret_cast<int*>(hA);
+            for (int h = c0; h < c1; h++) {
+                if (hE[h] == INT_MIN) { hslot[h] = su < kFbCap ? su : -1; su++; }
+                else hslot[h] = -1;
+            }
+        }
     }
     __syncthreads();
+    const int* hslot = reinterpret_cast<const int*>(hA);  // (with fb)
+    if (ph && threadIdx.x == 0) ph[1] = clock64();
     // transfer functions of predictable hot segments
-    for (int h0 = warp; h0 < nhot; h0 += kRowWarps * 4) {
+    Tf* htf0 = csize == 1 ? htf : cg::this_cluster().map_shared_rank(htf, 0);
+    for (int h0 = gw; h0 < nhot; h0 += nw * 4) {
         uint4 r[4];
         bool f[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-            const int h = h0 + u * kRowWarps;
-            f[u] = (h < nhot) && hE[h] != INT_MIN && rv.full(hot[h], lane);
+            const int h = h0 + u * nw;
+            f[u] = (h < nhot) && (hE[h] != INT_MIN || (fb && hslot[h] >= 0)) && rv.full(hot[h], lane);
             if (f[u]) r[u] = rv.raw(hot[h], lane);
         }
 #pragma unroll 1
         for (int u = 0; u < 4; u++) {
-            const int h = h0 + u * kRowWarps;
+            const int h = h0 + u * nw;
+            if (h < nhot && hE[h] == INT_MIN && fb && hslot[h] >= 0) {
+                // the exact terms the walk adds one by one (as walk_segment
+                // forms them), formed here in parallel
+                float v[EPL], dd[EPL], ex[EPL];
+                rv.widen(hot[h], lane, f[u], r[u], v);
+                const float thr = hthr[h];
+                uint32_t act = 0;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    const float t = __fmul_rn(v[e], inv);
+                    dd[e] = __fsub_rn(t, M);
+                    if (t >= thr) act |= 1u << e;
+                }
+                ref_expf_batch<EPL>(dd, act, ex, fx);
+                float* dst = fb + (size_t)hslot[h] * 256 + lane * EPL;
+#pragma unroll
+                for (int e = 0; e < EPL; e += 4)
+                    *reinterpret_cast<float4*>(dst + e) = make_float4(ex[e], ex[e + 1], ex[e + 2], ex[e + 3]);
+            }
             if (h < nhot && hE[h] != INT_MIN) {
                 const int E = hE[h];
                 float v[EPL];
@@ -780,15 +833,17 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                         if ((lane & (2 * o - 1)) == 0) tf = tf_compose(tf, b);
                     }
                 }
-                if (lane == 0) htf[h] = tf;
+                if (lane == 0) htf0[h] = tf;
             }
         }
     }
-    __syncthreads();
+    cluster_sync();
+    if (crank != 0) return;  // helpers: done
+    if (ph && threadIdx.x == 0) ph[11] = clock64();
     // the walk (warp 0) reproduces the sequential fp32 sum
     if (warp == 0) {
         float s = 0.0f;
-        int fb = 0;
+        int nfb = 0;
         int h = 0;
         while (h < nhot) {
             const int E = sum_binade(s);
@@ -814,12 +869,24 @@ __device__ __noinline__ void dense_sum(RowView<T> rv, int nseg, const float* seg
                 h += nok;
             }
             if (nok < 32 && h < nhot) {
-                s = walk_segment<T>(rv, hot[h], hthr[h], inv, M, s, wbuf, fx);
-                fb++;
+                if (fb && hE[h] == INT_MIN && hslot[h] >= 0) {
+                    // its exact terms are formed: add them in order
+                    const float* src = fb + (size_t)hslot[h] * 256 + lane * EPL;
+#pragma unroll
+                    for (int e = 0; e < EPL; e += 4)
+                        *reinterpret_cast<float4*>(wbuf + lane * EPL + e) = __ldcg(reinterpret_cast<const float4*>(src + e));
+                    __syncwarp();
+                    if (lane == 0) s = serial_sum(wbuf, 32 * EPL, s);
+                    s = __shfl_sync(0xffffffffu, s, 0);
+                    __syncwarp();
+                } else {
+                    s = walk_segment<T>(rv, hot[h], hthr[h], inv, M, s, wbuf, fx);
+                }
+                nfb++;
                 h++;
             }
         }
-        if (lane == 0) { sh->sum = s; sh->fb = fb; }
+        if (lane == 0) { sh->sum = s; sh->fb = nfb; }
     }
 }
 
@@ -1631,11 +1698,11 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
                   unsigned long long* __restrict__ rng, RowResult* __restrict__ res,
                   int* __restrict__ slow_list, int* __restrict__ slow_count,
                   int* __restrict__ cand_index_out, float* __restrict__ cand_prob_out, int cand_cap,
-                  ExpFix fx, int ccap, int scap, RowScratch scr, int nchunk,
+                  ExpFix fx, int ccap, int scap, RowScratch scr, int nchunk, int csize,
                   long long* __restrict__ phase_cycles) {
     constexpr int EPL = Elem<T>::kPerLane;
     constexpr int SEG = 32 * EPL;
-    const int row = blockIdx.x;
+    const int row = blockIdx.x / csize;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const RowSmem L(V, SEG, win.window, ccap, scap);
     const int nseg = L.nseg;
@@ -1660,7 +1727,10 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     __shared__ RowShared sh;
     const RowOut ro{res, slow_list, slow_count, cand_index_out, cand_prob_out, cand_cap, row};
 
-    long long* ph = phase_cycles ? phase_cycles + (size_t)row * 12 : nullptr;
+    // launched as clusters of csize CTAs (small batches), every CTA of a
+    // cluster takes the same row; only the first writes results
+    const int crank = (int)(blockIdx.x % (unsigned)csize);
+    long long* ph = (phase_cycles && crank == 0) ? phase_cycles + (size_t)row * 12 : nullptr;
     auto stamp = [&](int i) { if (ph && tid == 0) ph[i] = clock64(); };
     stamp(10);
     const float inv = __fdiv_rn(1.0f, prm.temperature);
@@ -1764,13 +1834,16 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
     if (tid == 0) {
         unsigned long long s = rng[row];
         sh.r = xorshift_f32(&s);
-        rng[row] = s;
+        if (crank == 0) rng[row] = s;  // (helper CTAs of a dense row only read it)
         sh.done = 0;
         sh.ncand = 0;
         sh.nknown = 0;
     }
     __syncthreads();
     const bool dense = sh.ovf != 0;
+    // a cluster's helper CTAs (rank > 0) only share the dense method's
+    // per-segment work: they leave at once when the row needs none
+    if (crank != 0 && !dense) return;
     const int nst = sh.nst;
     const float theta = __fsub_rn(fkey_inv(sh.maxlb), kSigGap);
     stamp(3);
@@ -1811,7 +1884,9 @@ row_finish_kernel(const T* __restrict__ logits, int V, RowParams prm, RowWindow 
         stamp(5);
         if (tid == 0) { sh.sum = serial_sum(slist, nst, 0.0f); sh.fb = -nst; }
     } else {
-        dense_sum<T>(rv, nseg, segm, inv, M, region, cd.ct, &sh, fx);
+        dense_sum<T>(rv, nseg, segm, inv, M, region, cd.ct, &sh, fx, ph, crank, csize,
+                     (scr.fb_terms && row < scr.fb_rows) ? scr.fb_terms + (size_t)row * kFbCap * 256 : nullptr);
+        if (crank != 0) return;  // the walk and everything after are the first CTA's
     }
     __syncthreads();
     const float sum = sh.sum;
@@ -2009,10 +2084,25 @@ cudaError_t launch_row_finish(const T* logits, int B, int V, RowParams prm, RowW
     cudaError_t err = cudaFuncSetAttribute(row_finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)L.total);
     if (err != cudaSuccess) return err;
-    row_finish_kernel<T><<<B, kRowThreads, L.total, stream>>>(logits, V, prm, win, rng, res, slow_list,
-                                                              slow_count, cand_index, cand_prob, cand_cap,
-                                                              fx, ccap, kStashCap, scr, nchunk, phase_cycles);
-    return cudaGetLastError();
+    // small batches leave SMs idle: each row gets a cluster whose helper CTAs
+    // share the dense method's per-segment work (rows whose stash settles the
+    // sum use only the first CTA)
+    const int csize = B <= 16 ? 8 : (B <= 64 ? 4 : (B <= 128 ? 2 : 1));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(B * csize));
+    cfg.blockDim = dim3(kRowThreads);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, row_finish_kernel<T>, logits, V, prm, win, rng, res, slow_list, slow_count,
+                              cand_index, cand_prob, cand_cap, fx, ccap, (int)kStashCap, scr, nchunk, csize,
+                              phase_cycles);
 }
 
 template cudaError_t launch_row_scan<float>(const float*, int, int, RowParams, RowWindow, RowResult*,
