@@ -385,8 +385,8 @@ def _kernel_split(s, run_pass, steps):
     torch.cuda.synchronize()
     pr = s.profile_read()
     s.profile(False)
-    return {"row_ms": pr["stream_ms"] / steps, "ties_ms": pr["ties_ms"] / steps,
-            "emit_ms": pr["emit_ms"] / steps}
+    return {"stream_ms": pr["stream_ms"] / steps, "finish_ms": pr["finish_ms"] / steps,
+            "ties_ms": pr["ties_ms"] / steps, "emit_ms": pr["emit_ms"] / steps}
 
 
 def measure_configs(torch, dev, steps: int, warmup: int, cpu: bool = True):
@@ -619,9 +619,9 @@ def main():
     sync_all()
     pr = s.profile_read()
     s.profile(False)
-    kms = {"row_ms": pr["stream_ms"] / args.steps, "ties_ms": pr["ties_ms"] / args.steps,
-           "emit_ms": pr["emit_ms"] / args.steps}
-    row_ms = pr["stream_ms"] / max(pr["row_launches"], 1)  # the row kernel: every logit once
+    kms = {"stream_ms": pr["stream_ms"] / args.steps, "finish_ms": pr["finish_ms"] / args.steps,
+           "ties_ms": pr["ties_ms"] / args.steps, "emit_ms": pr["emit_ms"] / args.steps}
+    row_ms = pr["stream_ms"] / max(pr["row_launches"], 1)  # the streaming pass: every logit once
     hbm, peak_kind = peaks()
     stream_ach = B * ROW_BYTES / (row_ms / 1e3) / 1e9
     step_ach = B * STEP_ROW_BYTES / (ms_step / 1e3) / 1e9
@@ -717,9 +717,9 @@ def main():
         "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": step_ach, "peak": hbm, "unit": "GB/s",
                      "frac": step_ach / hbm, "traffic": traffic, "peak_source": peak_kind,
-                     "kernel": "the sampling step (row, select, emit kernels)",
+                     "kernel": "the sampling step (streaming, finishing, tie-replay and emit kernels)",
                      "algorithmic_bytes_per_step": B * STEP_ROW_BYTES,
-                     "row_kernel": {"kernel": "qs::row_kernel<bf16> (chunk scans + each row's finish)",
+                     "row_kernel": {"kernel": "qs::wide::row_stream_kernel<bf16> (the streaming pass)",
                                     "kernel_ms": row_ms, "achieved": stream_ach, "frac": stream_ach / hbm,
                                     "algorithmic_bytes_per_launch": B * ROW_BYTES}},
         "kernel_ms_per_step": kms,

@@ -13,9 +13,11 @@
  *    sampler.h:298-317).  qs_last_error() gives a message for the calling
  *    thread.
  *  - Device pointers are owned by the caller and used on the caller's
- *    stream.  The library allocates device memory only in qs_build_sampler
- *    (workspace and per-row state sized for max_batch × vocab); sampling
- *    calls allocate nothing.
+ *    stream.  The library allocates device memory in qs_build_sampler
+ *    (workspace and per-row state sized for max_batch × vocab) and, on the
+ *    first call of a host entry point (qs_sample_host, qs_sample_rows_host),
+ *    that entry's fp32 staging buffer for max_batch × vocab logits; the
+ *    device sampling calls allocate nothing.
  *  - Logits are read only, unless QS_FLAG_WRITE_PENALIZED is set on an fp32
  *    call: then the penalised values are written back in place, as the
  *    reference's sample() does (sampler.h:125-138).

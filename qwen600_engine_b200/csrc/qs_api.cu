@@ -5,7 +5,8 @@
 //     per row, qs_row.cu) ->
 //   ties_kernel (rows whose draw depends on the reference's tie order) -> emit_kernel
 // on the caller's stream.  All device memory is allocated in
-// qs_build_sampler; the sampling entry points allocate nothing.
+// qs_build_sampler, except the host entry points' staging buffer (allocated
+// by their first call); the device entry points allocate nothing.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
@@ -330,7 +331,6 @@ int qs_build_sampler(qs_sampler** out, const qs_params* params, int max_batch, i
     s->fb_rows = (int)(B < (size_t)kWideMinRows ? B : (size_t)kWideMinRows);  // the chunked finish's rows
     ALLOC(s->rs_fb, sizeof(float) * 256 * kFbCap * (size_t)s->fb_rows);
     ALLOC(s->rs_gmax, sizeof(unsigned long long) * B);
-    ALLOC(s->d_in, sizeof(float) * B * V);
     ALLOC(s->st_hist, sizeof(int) * B * (size_t)s->ov_stride);
     ALLOC(s->st_counts, sizeof(float) * B * (size_t)s->ov_stride);
     ALLOC(s->st_count, sizeof(int) * B);
@@ -973,12 +973,22 @@ int qs_lm_head_set_wait_limit(unsigned long long ns) {
     return QS_OK;
 }
 
+// The host entry points' staging buffer for logits ([max_batch, vocab] fp32),
+// allocated by the first host-entry call so that handles used only with device
+// logits never hold it.
+static int host_staging(qs_sampler* s) {
+    if (s->d_in) return QS_OK;
+    CK(cudaMalloc(&s->d_in, sizeof(float) * (size_t)s->max_batch * s->vocab));
+    return QS_OK;
+}
+
 int qs_sample_host(qs_sampler* s, const float* h_logits, int batch, int* h_tokens, unsigned flags) {
     g_err.clear();
     if (!s || !h_logits || !h_tokens) return fail(QS_ERR_INVALID, "NULL argument");
     if (batch < 0 || batch > s->max_batch)
         return fail(QS_ERR_INVALID, "batch %d outside [0, %d]", batch, s->max_batch);
     DeviceGuard dg(s->device);
+    if (int rc0 = host_staging(s)) return rc0;
     CK(stage_h2d(s, s->d_in, h_logits, sizeof(float) * (size_t)batch * s->vocab, s->stream));
     int rc = qs_sample(s, s->d_in, QS_F32, batch, s->d_tok, s->stream, flags);
     if (rc) return rc;
@@ -1006,6 +1016,7 @@ int qs_sample_rows_host(qs_sampler* s, const void* h_logits, qs_dtype dtype, int
     cudaStream_t st = (cudaStream_t)stream;
     const size_t esz = dtype == QS_F32 ? 4 : 2;
     const size_t B = (size_t)batch, W = (size_t)window;
+    if (int rc0 = host_staging(s)) return rc0;
     CK(stage_h2d(s, s->d_in, h_logits, esz * B * (size_t)vocab, st));
     if (window > 0) {
         CK(cudaMemcpyAsync(s->st_hist, h_hist, sizeof(int) * B * W, cudaMemcpyHostToDevice, st));
