@@ -61,7 +61,8 @@ typedef enum { QS_F32 = 0, QS_BF16 = 1 } qs_dtype;
 
 /* Sampling parameters; field meanings as the reference Sampler's
  * (sampler.h:23-31).  top_k <= 0 or >= vocab means "no top-k" (full sort,
- * sampler.h:212-218). temperature < 1e-6 means greedy (sampler.h:178). */
+ * sampler.h:212-218); any top_k in between is served. temperature < 1e-6
+ * means greedy (sampler.h:178). */
 typedef struct {
     float temperature;
     float topp;
@@ -191,8 +192,8 @@ QS_API int qs_profile_reset(qs_sampler* s);
 QS_API int qs_profile_read(qs_sampler* s, qs_profile* out);
 
 /* Phase clocks for kernel tuning: with phases on, the row kernels record 12
- * clock64() stamps per row (which = 0) and the tie replay 16 per queued
- * row in queue order (which = 1), into device buffers that
+ * clock64() stamps per row (which = 0) and the tie replay 8 (in slots of
+ * 16) per queued row in queue order (which = 1), into device buffers that
  * qs_profile_phases_read copies out (n entries, synchronising the handle's
  * device first). */
 QS_API int qs_profile_phases(qs_sampler* s, int on);

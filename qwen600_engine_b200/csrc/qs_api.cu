@@ -512,8 +512,6 @@ static int run(qs_sampler* s, const Call& c) {
     if (c.batch == 0) return QS_OK;
     const bool greedy = p.temperature < 1e-6f;
     const bool topk = p.top_k > 0 && p.top_k < c.vocab;
-    if (!greedy && topk && p.top_k > kCandCap / 2)
-        return fail(QS_ERR_UNSUPPORTED, "top_k %d above this build's limit %d", p.top_k, kCandCap / 2);
     DeviceGuard dg(s->device);
     const int B = c.batch, V = c.vocab;
     const bool penalties = c.hist && c.hist_stride > 0 &&

@@ -33,6 +33,7 @@
 #include <cooperative_groups.h>
 
 #include "qs_common.cuh"
+#include "qs_radix.cuh"
 
 namespace qs {
 
@@ -42,7 +43,7 @@ constexpr int kTieCluster = 8;           // CTAs (SMs) per slow row
 constexpr int kTieThreads = 256;
 constexpr int kTieWarps = kTieThreads / 32;
 constexpr int kTieSmemRange = 2048;      // active ranges up to this size continue in shared memory
-constexpr int kTieSortCap = kCandCap / 2; // top-k limit of the API: the sorted prefix fits
+constexpr int kTieSortCap = kCandCap / 2; // top k sorted in shared memory; larger ones in global scratch
 #ifndef QS_TIE_UN
 #define QS_TIE_UN 8
 #endif
@@ -486,6 +487,51 @@ __host__ __device__ __forceinline__ int tie_mask_words(int V) {
     return (chunk + 31) / 32 + 1;
 }
 
+// The draw of a queued row whose top k exceeds kTieSortCap (the first CTA
+// alone, after the partition rounds; positions [0, k) of the row's
+// arrangement hold the selected entries): their exact probabilities
+// (sampler.h:197-206) as sort keys beside their indices, the stable sort of
+// the k by probability, descending (sampler.h:214; equal probabilities keep
+// position order, as glibc's stable qsort leaves them), then min-p / top-p /
+// renormalise / draw (sampler.h:144-162, 220-254).  The keys go to the row's
+// key array, the indices stay in place; the position arrays are the sort's
+// second buffer.  stg: kTieStage floats of shared memory (the passes'
+// histogram, then the serial walks' staging).
+constexpr int kTieStage = 4 * kTieSmemRange;
+template <typename T>
+__device__ __noinline__ void tie_draw_large(const T* __restrict__ L, int k, const GlobalArr& A, uint32_t* kB,
+                                            uint32_t* iB, const int* ovi, const float* ovv, int nov,
+                                            const RowResult& rr, const TieParams& prm, const ExpFix& fx,
+                                            float* stg, uint32_t* red, RowResult* res, int row,
+                                            int* cand_index_out, float* cand_prob_out, int cand_cap) {
+    uint32_t* kA = A.k;
+    uint32_t* iA = reinterpret_cast<uint32_t*>(A.idx);
+    for (int q = threadIdx.x; q < k; q += kTieThreads) {
+        const int t = A.index(q);
+        float l = Elem<T>::widen(L[t]);
+        int a = 0, b = nov;  // the override of t, if any (ovi ascending)
+        while (a < b) { const int m = (a + b) >> 1; if (ovi[m] < t) a = m + 1; else b = m; }
+        if (a < nov && ovi[a] == t) l = ovv[a];
+        __stcg(kA + q, sort_key(prob_of(__fmul_rn(l, rr.inv_temp), rr, fx)));
+    }
+    __syncthreads();
+    radix_sort<kTieWarps>(kA, iA, kB, iB, k, reinterpret_cast<uint32_t*>(stg), red);
+    const SortedDraw d = sorted_draw<kTieWarps, kTieStage>(kA, iA, k, prm.minp, prm.topp, rr.r, stg, red, row,
+                                                           cand_index_out, cand_prob_out, cand_cap);
+    if (threadIdx.x == 0) {
+        RowResult o = rr;
+        o.token = (int)__ldcg(iA + d.pos);
+        o.n_topk = k;
+        o.n_minp = d.n_minp;
+        o.n_final = d.n;
+        o.renorm_sum = d.s2;
+        o.draw_pos = d.pos;
+        o.exact_ties = 1;
+        o.status = 0;
+        res[row] = o;
+    }
+}
+
 template <typename T>
 __global__ void __cluster_dims__(kTieCluster, 1, 1) __launch_bounds__(kTieThreads, 3)
 ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __restrict__ ov_n,
@@ -528,7 +574,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
 
     for (int li = cid; li < nslow; li += ncl) {
         const int row = slow_list[li];
-        long long* ph = phase_cycles ? phase_cycles + (size_t)li * 8 : nullptr;
+        long long* ph = phase_cycles ? phase_cycles + (size_t)li * 16 : nullptr;
         if (ph && crank == 0 && tid == 0) ph[0] = clock64();
         const RowResult rr = res[row];
         const T* L = logits + (size_t)row * V;
@@ -611,12 +657,17 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
             // loop (identically in every CTA: all read the same values)
             if (lo < 0 || hi >= V || kk < lo || kk > hi) break;
         }
-        if (ph && crank == 0 && tid == 0) { ph[2] = clock64(); ph[6] = rounds; }
+        if (ph && crank == 0 && tid == 0) {
+            ph[2] = clock64(); ph[6] = rounds;
+        }
         // the rest is the first CTA's; when this cluster has no further row
         // the others leave now (none of them touches a peer's shared memory
         // again, and no cluster barrier follows), freeing their SMs
         const bool more = li + ncl < nslow;
-        if (!more && lo >= 0 && lo <= hi && hi < V) {
+        // (a top k above kTieSortCap reuses the key and position arrays for
+        // its sort: nothing is dropped then, since the others' drops could
+        // land after the first CTA's writes)
+        if (!more && k <= kTieSortCap && lo >= 0 && lo <= hi && hi < V) {
             // After the cluster's last row only the first CTA reads the
             // scratch again, and only keys [lo, hi] and indices [0, max(k, hi + 1)):
             // every CTA drops its share of the rest from L2 (the position
@@ -672,6 +723,13 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                 __syncthreads();
             }
             if (ph && tid == 0) { ph[3] = clock64(); ph[7] = rounds; }
+            if (k > kTieSortCap) {
+                tie_draw_large<T>(L, k, A, reinterpret_cast<uint32_t*>(gposL.p),
+                                  reinterpret_cast<uint32_t*>(gposR.p), ovi, ovv, nov, rr, prm, fx,
+                                  reinterpret_cast<float*>(sK), reinterpret_cast<uint32_t*>(red), res, row,
+                                  cand_index_out, cand_prob_out, cand_cap);
+                if (ph && tid == 0) ph[4] = clock64();
+            } else {
             // exact probabilities of the k selected entries (sampler.h:197-206),
             // then the stable qsort of the first k by probability, descending
             // (sampler.h:214): keys (p, k-1-position) keep equal p in position order
@@ -746,6 +804,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                         cand_prob_out[(size_t)row * cand_cap + i] = i < n ? __fmul_rn(P(i), inv2) : P(i);
                     }
                 }
+            }
             }
         }
         // the scratch and the exchange slots are reused by the next row

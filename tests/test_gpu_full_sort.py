@@ -70,13 +70,14 @@ def test_full_sort_against_reference(ref_sampler):
     np.testing.assert_array_equal(g["cand_index"], o["index"][:, :64])
 
 
-def test_index_ties_topk_overflow(oracle):
+@pytest.mark.parametrize("k", [1000, 4000])
+def test_index_ties_topk_overflow(oracle, k):
     """Top-k beyond the candidate buffer under QS_FLAG_INDEX_TIES (ties in
     index order): the full sort takes the first k.  fp32 normal rows hold no
     equal probabilities, so the reference's order is the same."""
     torch_mod()
     from qwen600_engine_b200.sampler import QS_FLAG_INDEX_TIES
-    p = W.SamplingParams(1.0, 0.97, 0.0, 1000, 1.0, 0.0, 0.0)
+    p = W.SamplingParams(1.0, 0.97, 0.0, k, 1.0, 0.0, 0.0)
     wl = flat(W.VOCAB, "f32", p, B=4, seed=33)
     o = oracle.sample_workload(wl, debug=True, cand_cap=64)
     g = run_gpu(wl, flags=QS_FLAG_INDEX_TIES, cand_cap=64)

@@ -169,7 +169,36 @@ CASES = {
     # penalties)
     "nucleus_f32_320_streamed": lambda: W.nucleus_f32(B=320, seed=31),
     "greedy_f32_300_streamed": lambda: _greedy_f32(300),
+    # top k above the tie replay's shared-memory sort (1024): every such row
+    # is queued and its k entries sorted in global memory
+    "topk3000_bf16_12": lambda: _large_k(W.topk_bf16(B=12, seed=41), (0.7, 1.0, 0.0, 3000, 1.15, 0.0, 0.0)),
+    "topk1500_f32_16": lambda: _large_k(_normal_f32(16, 43, 1.5), (0.35, 0.9, 0.0, 1500, 1.2, 0.5, 0.3)),
+    "topk2000_bf16_256_streamed": lambda: _large_k(W.topk_bf16(B=256, seed=45),
+                                                   (2.0, 0.97, 0.0, 2000, 1.1, 0.0, 0.0)),
+    "topk5000_ties_f32_8": lambda: _large_k(_rounded_f32(8, 47), (1.0, 0.98, 0.01, 5000, 1.0, 0.0, 0.0)),
 }
+
+
+def _large_k(wl, params):
+    wl.params = W.SamplingParams(*params)
+    return wl
+
+
+def _normal_f32(B, seed, scale):
+    wl = W.nucleus_f32(B=B, seed=seed)
+    g = np.random.default_rng(seed)
+    wl.logits = (scale * g.standard_normal(wl.logits.shape)).astype(np.float32)
+    return wl
+
+
+def _rounded_f32(B, seed):
+    """Logits rounded to multiples of 0.5 (thousands of exact ties at every
+    rank), the first row all equal."""
+    wl = W.nucleus_f32(B=B, seed=seed)
+    g = np.random.default_rng(seed)
+    wl.logits = np.round(2.0 * g.standard_normal(wl.logits.shape)).astype(np.float32) * np.float32(0.5)
+    wl.logits[0] = 0.0
+    return wl
 
 
 def _greedy_f32(B):
@@ -213,7 +242,8 @@ def test_golden_vectors_on_gpu():
                              f"{name} row {r}")
 
 
-@pytest.mark.parametrize("name", ["single_row_x24", "topk_bf16_192", "nucleus_f32_24"])
+@pytest.mark.parametrize("name", ["single_row_x24", "topk_bf16_192", "nucleus_f32_24", "topk3000_bf16_12",
+                                  "topk5000_ties_f32_8"])
 def test_probabilities_and_candidates(oracle, name):
     wl = CASES[name]()
     rows = min(wl.batch, 6)
