@@ -277,7 +277,12 @@ QS_API int qs_ipc_free(void* d_ptr);
  * resulting bf16 logits: the reference's forward() tail plus sample()
  * (main.cu:138-139) for a batch, without the fp32 widening and the host copy
  * of qwen_model.cuh:717-723.  The first call (and a call with a new
- * hidden_dim) allocates the workspace: max_batch x (hidden_dim + vocab) bf16.
+ * hidden_dim) allocates the workspace: max_batch x (hidden_dim + vocab) bf16,
+ * plus min(max_batch, 255) x ceil(vocab / 256) words for the segment maxima.
+ * For batches below 256 the lm_head epilogue folds each row's maxima of its
+ * 256-column segments into that buffer, and the sampler then reads only the
+ * segments that hold window tokens from the logits instead of streaming them
+ * (same tokens as qs_sample on the same logits).
  * qs_lm_head_logits returns that logits buffer (for inspection);
  * qs_lm_head_status synchronises `stream` and reports (and clears) the
  * kernel's give-up flag. */

@@ -58,7 +58,7 @@ cudaError_t launch_probs(const T*, int, int, const int*, const int*, const float
                          const RowResult*, float*, ExpFix, cudaStream_t);
 
 cudaError_t launch_lm_head(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int, int,
-                           int, int*, cudaStream_t);
+                           int, int*, cudaStream_t, uint32_t*, int);
 cudaError_t launch_rmsnorm(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int,
                            cudaStream_t);
 void lm_head_set_wait_ns(unsigned long long);
@@ -141,6 +141,8 @@ struct qs_sampler {
     __nv_bfloat16* lh_normed = nullptr;  // [max_batch, lh_dim]
     __nv_bfloat16* lh_logits = nullptr;  // [max_batch, vocab]
     int* lh_err = nullptr;
+    uint32_t* lh_segk = nullptr;  // [max_batch, lh_segs]: the epilogue's segment maxima (order keys)
+    int lh_segs = 0;
     ExpFix fix() const { return ExpFix{exp_off, exp_ent, exp_bloom, (uint32_t)QS_EXP_NB}; }
     // the row kernel's hand-over from a row's chunk scans to its finishing CTA
     float* rs_segm = nullptr;
@@ -224,7 +226,7 @@ static void release(qs_sampler* s) {
     void* ptrs[] = {s->ov_n, s->ov_idx, s->ov_val, s->res, s->slow_list, s->slow_count,
                     s->tie_scratch, s->tie_pos, s->ring, s->hcount, s->hpos, s->token_counts, s->slot_counts,
                     s->rng, s->d_in, s->d_tok, s->exp_off, s->exp_ent, s->exp_bloom,
-                    s->lh_normed, s->lh_logits, s->lh_err, s->rs_segm, s->rs_done,
+                    s->lh_normed, s->lh_logits, s->lh_err, s->lh_segk, s->rs_segm, s->rs_done,
                     s->rs_gmax, s->rs_stash, s->rs_used, s->rs_chunk, s->rs_chunk_lb, s->rs_fb, s->st_hist, s->st_counts, s->st_count, s->st_rng, s->ph_row, s->ph_sel};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -476,6 +478,8 @@ struct Call {
     float* ring_counts;
     cudaStream_t stream;
     unsigned flags;
+    uint32_t* premax;     // bf16 rows' segment maxima formed by the lm_head epilogue (or nullptr)
+    int premax_stride;
 };
 
 // Host-to-device copy of `bytes` in kCopyChunks pieces over the copy streams,
@@ -545,9 +549,13 @@ static int run(qs_sampler* s, const Call& c) {
                                                       s->scratch(), c.stream, s->ph_row));
         else if (c.dtype == QS_F32)
             CK(launch_row_scan<float>((const float*)c.logits, B, V, rp, win, s->res, s->scratch(), c.stream));
-        else
-            CK(launch_row_scan<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, s->res,
-                                              s->scratch(), c.stream));
+        else {
+            RowScratch scr = s->scratch();
+            scr.premax = c.premax;
+            scr.premax_stride = c.premax_stride;
+            CK(launch_row_scan<__nv_bfloat16>((const __nv_bfloat16*)c.logits, B, V, rp, win, s->res, scr,
+                                              c.stream));
+        }
     }
     if (!greedy) {
         KernelScope ks(s, 1, c.stream);
@@ -634,11 +642,12 @@ static int run(qs_sampler* s, const Call& c) {
 
 extern "C" {
 
-int qs_sample(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, int* d_tokens,
-              void* stream, unsigned flags) {
-    g_err.clear();
-    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+// The stateful call; premax: segment maxima the lm_head epilogue formed for
+// these bf16 rows (batches below kWideMinRows only).
+static int sample_stateful(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, int* d_tokens,
+                           void* stream, unsigned flags, uint32_t* premax, int premax_stride) {
     Call c{};
+    c.premax = premax; c.premax_stride = premax_stride;
     c.logits = d_logits; c.dtype = dtype; c.batch = batch; c.vocab = s->vocab;
     c.hist = s->ring; c.hist_stride = s->window; c.hist_count = s->hcount;
     c.slot_counts = s->slot_counts;
@@ -647,6 +656,13 @@ int qs_sample(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, in
     c.ring_counts = s->slot_counts;
     c.stream = (cudaStream_t)stream; c.flags = flags;
     return run(s, c);
+}
+
+int qs_sample(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, int* d_tokens,
+              void* stream, unsigned flags) {
+    g_err.clear();
+    if (!s) return fail(QS_ERR_INVALID, "sampler is NULL");
+    return sample_stateful(s, d_logits, dtype, batch, d_tokens, stream, flags, nullptr, 0);
 }
 
 int qs_sample_rows_debug(qs_sampler* s, const void* d_logits, qs_dtype dtype, int batch, int vocab,
@@ -775,7 +791,8 @@ static int lm_head_args(const void* d_hidden, const void* d_weight, int batch, i
 // streams W once).
 static int lm_head_launch(const void* d_hidden, const void* d_norm_weight, const void* d_weight,
                           int batch, int hidden_dim, int vocab, __nv_bfloat16* normed,
-                          __nv_bfloat16* logits, int* err, int num_sms, cudaStream_t st) {
+                          __nv_bfloat16* logits, int* err, int num_sms, cudaStream_t st,
+                          uint32_t* segk = nullptr, int segk_stride = 0) {
     if (batch == 0) return QS_OK;
     CK(launch_rmsnorm((const __nv_bfloat16*)d_hidden, (const __nv_bfloat16*)d_norm_weight, normed,
                       batch, hidden_dim, st));
@@ -784,7 +801,8 @@ static int lm_head_launch(const void* d_hidden, const void* d_norm_weight, const
         const cudaError_t e = launch_lm_head(normed + (size_t)r0 * hidden_dim,
                                              (const __nv_bfloat16*)d_weight,
                                              logits + (size_t)r0 * vocab, rb, vocab, hidden_dim,
-                                             num_sms, err, st);
+                                             num_sms, err, st,
+                                             segk ? segk + (size_t)r0 * segk_stride : nullptr, segk_stride);
         if (e == cudaErrorInvalidValue)
             return fail(QS_ERR_UNSUPPORTED, "lm_head: the tensor maps of these buffers cannot be built");
         CK(e);
@@ -937,10 +955,22 @@ int qs_lm_head_sample(qs_sampler* s, const void* d_hidden, const void* d_norm_we
         CK(cudaMemset(s->lh_err, 0, sizeof(int)));
         s->lh_dim = hidden_dim;
     }
+    if (!s->lh_segk) {
+        s->lh_segs = (s->vocab + 255) / 256;
+        const size_t n = (size_t)(s->max_batch < kWideMinRows ? s->max_batch : kWideMinRows - 1) * s->lh_segs;
+        CK(cudaMalloc(&s->lh_segk, sizeof(uint32_t) * n));
+        CK(cudaMemset(s->lh_segk, 0, sizeof(uint32_t) * n));
+    }
+    // batches below kWideMinRows: the epilogue forms the segment maxima and
+    // the sampler's scan reads only the window's segments from the logits
+    uint32_t* segk = batch < kWideMinRows ? s->lh_segk : nullptr;
     rc = lm_head_launch(d_hidden, d_norm_weight, d_weight, batch, hidden_dim, s->vocab, s->lh_normed,
-                        s->lh_logits, s->lh_err, s->num_sms, (cudaStream_t)stream);
+                        s->lh_logits, s->lh_err, s->num_sms, (cudaStream_t)stream, segk, s->lh_segs);
     if (rc) return rc;
-    return qs_sample(s, s->lh_logits, QS_BF16, batch, d_tokens, stream, flags);
+    rc = sample_stateful(s, s->lh_logits, QS_BF16, batch, d_tokens, stream, flags, segk, s->lh_segs);
+    if (rc && segk)  // the scan did not consume (and zero) the maxima
+        cudaMemsetAsync(segk, 0, sizeof(uint32_t) * (size_t)batch * s->lh_segs, (cudaStream_t)stream);
+    return rc;
 }
 
 int qs_lm_head_logits(qs_sampler* s, const void** d_logits) {

@@ -66,6 +66,12 @@ struct RowScratch {
     // cannot be predicted, formed in parallel before the sequential walk
     float* fb_terms;           // [fb_rows][kFbCap][256]
     int fb_rows;               // rows it has room for (0: none; the walk forms them itself)
+    // bf16 rows whose producer already formed the segment maxima (the lm_head
+    // epilogue): order keys (fkey) of the raw maxima of the full 256-element
+    // segments, [rows][premax_stride]; the scan reads them instead of
+    // streaming the row and leaves the buffer zeroed.  nullptr: stream.
+    uint32_t* premax;
+    int premax_stride;
 };
 constexpr int kFbCap = 64;      // segments per row with precomputed exact terms
 // Segment maxima per row that fit either element type (fp32 segments are the
@@ -156,6 +162,26 @@ __device__ __forceinline__ uint32_t fkey(float f) { return fkey_bits(__float_as_
 __device__ __forceinline__ float fkey_inv(uint32_t k) {
     uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
     return __uint_as_float(u);
+}
+
+// Maximum of one 16-byte vector of logits (a lane's share of a segment; bf16
+// pairs compared packed).  The streaming passes and the lm_head epilogue form
+// segment maxima with it, so both give the same bits.
+template <typename T>
+__device__ __forceinline__ float vec_max(const uint4& r);
+template <>
+__device__ __forceinline__ float vec_max<__nv_bfloat16>(const uint4& r) {
+    __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
+    __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
+    __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&r.z);
+    __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&r.w);
+    __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
+    return fmaxf(__low2float(m), __high2float(m));
+}
+template <>
+__device__ __forceinline__ float vec_max<float>(const uint4& r) {
+    return fmaxf(fmaxf(__uint_as_float(r.x), __uint_as_float(r.y)),
+                 fmaxf(__uint_as_float(r.z), __uint_as_float(r.w)));
 }
 
 // ------------------------------------------------------------- reductions

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
 lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int tma_out, __nv_bfloat16* __restrict__ out, int B,
                int V, int K, int ntiles, int* __restrict__ err, const __grid_constant__ LhPeer peer,
-               unsigned long long wait_ns) {
+               unsigned long long wait_ns, uint32_t* __restrict__ segk, int segk_stride) {
     using Tl = LhTile<N>;
     constexpr uint32_t kLhStageB = Tl::kStageB;
     constexpr uint32_t kLhOutTile = Tl::kOutTile;
@@ -251,6 +251,10 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (tma_out && lane == 0)  // the previous tile's store has read the staging rows
                 asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             __syncwarp();
+            // the row's running segment maximum (order key) over this tile's
+            // columns; 16-column pieces never straddle a 256-column segment
+            uint32_t run = 0u;
+            int rseg = n0 >> 8;
 #pragma unroll 1
             for (int c = 0; c < kLhN / 16; c++) {
                 uint32_t r[16];
@@ -261,6 +265,20 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]),
                                                                   __uint_as_float(r[2 * j + 1]));
                     pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                if (segk && n0 + c * 16 < V) {
+                    const int sg = (n0 + c * 16) >> 8;
+                    if (sg != rseg) {
+                        if (run && row < B) atomicMax(segk + (size_t)row * segk_stride + rseg, run);
+                        run = 0u;
+                        rseg = sg;
+                    }
+                    if (n0 + c * 16 + 16 <= V) {
+                        // per 8 columns, as a streaming lane forms them
+                        const uint32_t k1 = fkey(vec_max<__nv_bfloat16>(make_uint4(pk[0], pk[1], pk[2], pk[3])));
+                        const uint32_t k2 = fkey(vec_max<__nv_bfloat16>(make_uint4(pk[4], pk[5], pk[6], pk[7])));
+                        run = max(run, max(k1, k2));
+                    }
                 }
                 if (staged) {
                     uint4* d4 = reinterpret_cast<uint4*>(stage + c * 16);
@@ -281,6 +299,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                 }
             }
+            if (run && row < B) atomicMax(segk + (size_t)row * segk_stride + rseg, run);
             tc_fence_before();
             if (tma_out) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
@@ -391,7 +410,8 @@ static bool make_map(CUtensorMap* m, const void* ptr, int rows, int K, int box_r
 
 template <int N>
 static cudaError_t lm_head_go(const CUtensorMap& ma, const __nv_bfloat16* W, __nv_bfloat16* logits, int B,
-                              int V, int K, int num_sms, int* err, const LhPeer& peer, cudaStream_t stream) {
+                              int V, int K, int num_sms, int* err, const LhPeer& peer, uint32_t* segk,
+                              int segk_stride, cudaStream_t stream) {
     CUtensorMap mb;
     if (!make_map(&mb, W, V, K, N)) return cudaErrorInvalidValue;
     // the logits as [B, V] with 32-row x N-column boxes, unswizzled (row
@@ -415,7 +435,7 @@ static cudaError_t lm_head_go(const CUtensorMap& ma, const __nv_bfloat16* W, __n
     cudaError_t e = cudaFuncSetAttribute(lm_head_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     lm_head_kernel<N><<<grid, kLhThreads, smem, stream>>>(ma, mb, mc, tma_out, logits, B, V, K, ntiles, err, peer,
-                                                            g_wait_ns);
+                                                            g_wait_ns, segk, segk_stride);
     return cudaGetLastError();
 }
 
@@ -435,31 +455,35 @@ int lm_head_tile(int V, int num_sms) {
 
 static cudaError_t lm_head_dispatch(const __nv_bfloat16* normed, const __nv_bfloat16* W, __nv_bfloat16* logits,
                                     int B, int V, int K, int num_sms, int* err, const LhPeer& peer,
-                                    cudaStream_t stream) {
+                                    uint32_t* segk, int segk_stride, cudaStream_t stream) {
     CUtensorMap ma;
     if (!make_map(&ma, normed, B, K, kLhM)) return cudaErrorInvalidValue;
     switch (lm_head_tile(V, num_sms)) {
-        case 176: return lm_head_go<176>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
-        case 144: return lm_head_go<144>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
-        case 128: return lm_head_go<128>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
-        default: return lm_head_go<208>(ma, W, logits, B, V, K, num_sms, err, peer, stream);
+        case 176: return lm_head_go<176>(ma, W, logits, B, V, K, num_sms, err, peer, segk, segk_stride, stream);
+        case 144: return lm_head_go<144>(ma, W, logits, B, V, K, num_sms, err, peer, segk, segk_stride, stream);
+        case 128: return lm_head_go<128>(ma, W, logits, B, V, K, num_sms, err, peer, segk, segk_stride, stream);
+        default: return lm_head_go<208>(ma, W, logits, B, V, K, num_sms, err, peer, segk, segk_stride, stream);
     }
 }
 
 // logits[B, V] = bf16(normed[B, K] . W[V, K]^T); B <= 128, K % 64 == 0.
+// With segk, the epilogue also folds each row's raw maxima of the 256-column
+// segments into segk[row * segk_stride + segment] (atomicMax of order keys;
+// the buffer starts zeroed and the sampler's scan zeroes it again).
 // Returns cudaErrorInvalidValue when a tensor map cannot be built.
 cudaError_t launch_lm_head(const __nv_bfloat16* normed, const __nv_bfloat16* W, __nv_bfloat16* logits,
-                           int B, int V, int K, int num_sms, int* err, cudaStream_t stream) {
+                           int B, int V, int K, int num_sms, int* err, cudaStream_t stream, uint32_t* segk,
+                           int segk_stride) {
     LhPeer none;
     memset(&none, 0, sizeof(none));
-    return lm_head_dispatch(normed, W, logits, B, V, K, num_sms, err, none, stream);
+    return lm_head_dispatch(normed, W, logits, B, V, K, num_sms, err, none, segk, segk_stride, stream);
 }
 
 // One vocabulary slice: logits of W_shard's `cols` rows for B <= 128 batch
 // rows, each stored to the rank that samples it (see LhPeer).
 cudaError_t launch_lm_head_shard(const __nv_bfloat16* normed, const __nv_bfloat16* W_shard, int B, int cols,
                                  int K, int num_sms, int* err, const LhPeer& peer, cudaStream_t stream) {
-    return lm_head_dispatch(normed, W_shard, nullptr, B, cols, K, num_sms, err, peer, stream);
+    return lm_head_dispatch(normed, W_shard, nullptr, B, cols, K, num_sms, err, peer, nullptr, 0, stream);
 }
 
 cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int B, int D,

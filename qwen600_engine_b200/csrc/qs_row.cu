@@ -249,24 +249,6 @@ struct RowView {
     }
 };
 
-// Lane maximum of one vector (raw bf16 pairs compared packed).
-template <typename T>
-__device__ __forceinline__ float vec_max(const uint4& r);
-template <>
-__device__ __forceinline__ float vec_max<__nv_bfloat16>(const uint4& r) {
-    __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
-    __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
-    __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&r.z);
-    __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&r.w);
-    __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
-    return fmaxf(__low2float(m), __high2float(m));
-}
-template <>
-__device__ __forceinline__ float vec_max<float>(const uint4& r) {
-    return fmaxf(fmaxf(__uint_as_float(r.x), __uint_as_float(r.y)),
-                 fmaxf(__uint_as_float(r.z), __uint_as_float(r.w)));
-}
-
 // ------------------------------------------------------------- block helpers
 // Barrier of the threads that run a row pass (the whole CTA); the block
 // helpers take it as a parameter.
@@ -1355,11 +1337,15 @@ row_scan_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, 
     const int g0 = chunk * kRowChunkSegs;
     const int lo_idx = g0 * SEG;
     const int hi_idx = min(V, (g0 + kRowChunkSegs) * SEG);
+    // maxima formed by the producer: only the window's segments and the
+    // partial last one are read from the row
+    uint32_t* pre_row = scr.premax ? scr.premax + (size_t)row * scr.premax_stride : nullptr;
+    const bool pre = pre_row && !greedy;
     uint4 rs[US];
 #pragma unroll
     for (int u = 0; u < US; u++) {
         const int g = g0 + warp + u * kRowWarps;
-        rs[u] = (g < nseg && rv.full(g, lane)) ? rv.raw(g, lane) : make_uint4(0u, 0u, 0u, 0u);
+        rs[u] = (!pre && g < nseg && rv.full(g, lane)) ? rv.raw(g, lane) : make_uint4(0u, 0u, 0u, 0u);
     }
     if (tid == 0) s_best = 0ull;
     // the window while the chunk's loads are in flight
@@ -1382,12 +1368,15 @@ row_scan_kernel(const T* __restrict__ logits, int V, int nchunk, RowParams prm, 
         float v[EPL];
         bool have = false;
         if (!greedy && !wseg && rv.aligned && base + SEG <= V) {
-            const float m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(vec_max<T>(rs[u]))));
+            const float m = pre ? fkey_inv(__ldcg(pre_row + g))
+                                : fkey_inv(__reduce_max_sync(0xffffffffu, fkey(vec_max<T>(rs[u]))));
             if (lane == 0) scr.segm[(size_t)row * scr.seg_stride + g] = m;
         } else {
+            if (pre && rv.full(g, lane)) rs[u] = rv.raw(g, lane);
             rv.widen_raw(g, lane, rv.full(g, lane), rs[u], v);
             have = true;
         }
+        if (pre_row && lane == 0) pre_row[g] = 0u;  // zeroed for the producer's next call
         if (!have) continue;
         const int lb = base + lane * EPL;
         if (wseg) {

@@ -250,24 +250,6 @@ struct RowView {
     }
 };
 
-// Lane maximum of one vector (raw bf16 pairs compared packed).
-template <typename T>
-__device__ __forceinline__ float vec_max(const uint4& r);
-template <>
-__device__ __forceinline__ float vec_max<__nv_bfloat16>(const uint4& r) {
-    __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
-    __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
-    __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&r.z);
-    __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&r.w);
-    __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
-    return fmaxf(__low2float(m), __high2float(m));
-}
-template <>
-__device__ __forceinline__ float vec_max<float>(const uint4& r) {
-    return fmaxf(fmaxf(__uint_as_float(r.x), __uint_as_float(r.y)),
-                 fmaxf(__uint_as_float(r.z), __uint_as_float(r.w)));
-}
-
 // ------------------------------------------------------------- block helpers
 __device__ __forceinline__ float rblock_max(float v, float* red) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;

@@ -124,6 +124,41 @@ def test_lm_head_sample_matches_reference_sampler_on_emitted_logits(ref_sampler)
     sess.free()
 
 
+@pytest.mark.parametrize("B,V,params", [
+    (128, W.VOCAB, (0.6, 0.95, 0.05, 20, 1.1, 0.5, 0.3)),   # penalised window tokens, tile 208
+    (130, 37984, (0.8, 0.9, 0.0, 0, 1.2, 0.0, 0.0)),        # two 128-row launches, tile 144, no top-k
+    (7, 4096, (0.0, 1.0, 0.0, 0, 1.3, 0.0, 0.2)),           # greedy rows, tile 128
+])
+def test_lm_head_sample_epilogue_maxima_match_streamed(B, V, params):
+    """qs_lm_head_sample takes the rows' segment maxima from the lm_head
+    epilogue and reads only the window's segments from the logits; sampling
+    the same logits with qs_sample (which streams them) must give the same
+    tokens and RNG states, step after step (the scan zeroes the epilogue's
+    buffer for the next call, and the sampled tokens enter the windows)."""
+    torch = _torch()
+    from qwen600_engine_b200.sampler import Sampler
+    D = 1024
+    p = W.SamplingParams(*params)
+
+    def make():
+        return Sampler(p.temperature, p.topp, p.minp, p.top_k, p.repetition_penalty, p.frequency_penalty,
+                       p.presence_penalty, 64, 5, max_batch=B, vocab=V)
+    fused, plain = make(), make()
+    _, w, nw = _inputs(torch, 1, D, V, seed=21)
+    for step in range(4):
+        h, _, _ = _inputs(torch, B, D, 8, seed=300 + step, norm_weight=False)
+        tok = fused.lm_head_sample(h, w, nw)
+        torch.cuda.synchronize()
+        fused.lm_head_status()
+        logits = fused.lm_head_logits(B).clone()
+        want = plain.sample(logits)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(tok.cpu().numpy(), want.cpu().numpy(), err_msg=f"step {step}")
+    np.testing.assert_array_equal(fused.rng_state, plain.rng_state)
+    fused.free()
+    plain.free()
+
+
 def test_lm_head_argument_errors():
     torch = _torch()
     from qwen600_engine_b200.sampler import SamplerError, lm_head
