@@ -336,8 +336,8 @@ def measure_lm_head_sharded(torch, dev, rank, world, B=128, K=1024, iters=20):
             "us_per_step": res[False], "with_sampling_us": res[True],
             "rows_per_s_with_sampling": B / (res[True] * 1e-6),
             "whole_job_GBps": byts / (res[False] * 1e-6) / 1e9,
-            "note": "max over ranks of CUDA-event time; the step includes the completion barrier "
-                    "(one-element NCCL all-reduce)"}
+            "note": "max over ranks of CUDA-event time; the step includes the completion handshake "
+                    "(device-side flag words over NVLink, qs_shard_handshake)"}
 
 
 def _wl_to_dev(torch, wl, dev):

@@ -249,8 +249,8 @@ QS_API int qs_lm_head(const void* d_hidden, const void* d_norm_weight, const voi
  * b / rows_per_rank: each logit row segment is stored straight into that
  * rank's buffer d_row_dst[rank] (bf16 [rows_per_rank, vocab], row
  * b % rows_per_rank, columns col0 ..), over NVLink for the other ranks, so
- * once every rank's call has completed (a barrier on the stream, e.g. a
- * one-element NCCL all-reduce) each rank holds whole logit rows, bit-identical
+ * once every rank's call has completed (qs_shard_handshake on the stream,
+ * or any cross-rank barrier) each rank holds whole logit rows, bit-identical
  * to qs_lm_head's, for the sampler.  d_row_dst is a host array of nranks
  * device pointers: this rank's own buffer and the peers' buffers mapped with
  * qs_ipc_open.  vocab, col0 and shard_cols multiples of 8; nranks <= 8;
@@ -267,6 +267,22 @@ QS_API int qs_lm_head_shard(const void* d_hidden, const void* d_norm_weight, con
  * handle (qs_ipc_handle_bytes() bytes) to `handle`; another process passes
  * that handle to qs_ipc_open to get a pointer it can store to, and releases
  * it with qs_ipc_close; the owner frees the buffer with qs_ipc_free. */
+/* Completion handshake of a vocabulary-sharded launch, enqueued on `stream`
+ * after qs_lm_head_shard: one small kernel publishes `epoch` to every rank
+ * (this rank's peer stores before it become visible first) and waits until
+ * every rank has published `epoch` for this call; then this rank's rows are
+ * whole.  d_bufs: the nranks buffers of qs_lm_head_shard's d_row_dst (each
+ * allocated with qs_ipc_alloc, which zeroes it); each holds nranks 32-bit
+ * flag words at byte offset flag_offset (a multiple of 16, past the rows).
+ * epoch: 1 on the first call, one more per call (the same on every rank).
+ * The wait gives up after limit_ns (0: 2 s), sets *d_error_flag to 1 and
+ * returns, so a rank that never arrives is reported instead of waited for.
+ * Every rank must have finished reading its rows of call e before any rank
+ * starts call e + 1 (its stores land in the peers' rows).  No counterpart in
+ * the reference (which runs on one GPU). */
+QS_API int qs_shard_handshake(void* const* d_bufs, int nranks, int rank, size_t flag_offset, unsigned epoch,
+                              unsigned long long limit_ns, int* d_error_flag, void* stream);
+
 QS_API int qs_ipc_handle_bytes(void);
 QS_API int qs_ipc_alloc(size_t bytes, void** d_ptr, void* handle);
 QS_API int qs_ipc_open(const void* handle, void** d_ptr);

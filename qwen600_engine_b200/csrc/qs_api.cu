@@ -62,6 +62,8 @@ cudaError_t launch_lm_head(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bflo
 cudaError_t launch_rmsnorm(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int,
                            cudaStream_t);
 void lm_head_set_wait_ns(unsigned long long);
+cudaError_t launch_shard_handshake(void* const*, size_t, int, int, unsigned, unsigned long long, int*,
+                                   cudaStream_t);
 cudaError_t launch_lm_head_shard(const __nv_bfloat16*, const __nv_bfloat16*, int, int, int, int, int*,
                                  const LhPeer&, cudaStream_t);
 
@@ -899,6 +901,13 @@ int qs_ipc_alloc(size_t bytes, void** d_ptr, void* handle) {
     *d_ptr = nullptr;
     void* p = nullptr;
     CK(cudaMalloc(&p, bytes));
+    {
+        const cudaError_t z = cudaMemset(p, 0, bytes);  // flag words start at zero
+        if (z != cudaSuccess) {
+            cudaFree(p);
+            return fail(QS_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(z));
+        }
+    }
     cudaIpcMemHandle_t h;
     const cudaError_t e = cudaIpcGetMemHandle(&h, p);
     if (e != cudaSuccess) {
@@ -931,6 +940,22 @@ int qs_ipc_free(void* d_ptr) {
     g_err.clear();
     if (!d_ptr) return QS_OK;
     CK(cudaFree(d_ptr));
+    return QS_OK;
+}
+
+int qs_shard_handshake(void* const* d_bufs, int nranks, int rank, size_t flag_offset, unsigned epoch,
+                       unsigned long long limit_ns, int* d_error_flag, void* stream) {
+    g_err.clear();
+    if (!d_bufs || !d_error_flag) return fail(QS_ERR_INVALID, "NULL argument");
+    if (nranks < 1 || nranks > kLhMaxRanks)
+        return fail(QS_ERR_UNSUPPORTED, "nranks %d outside [1, %d]", nranks, kLhMaxRanks);
+    if (rank < 0 || rank >= nranks) return fail(QS_ERR_INVALID, "rank %d outside [0, %d)", rank, nranks);
+    if (flag_offset % 16) return fail(QS_ERR_INVALID, "flag_offset must be a multiple of 16");
+    for (int r = 0; r < nranks; r++)
+        if (!d_bufs[r]) return fail(QS_ERR_INVALID, "buffer of rank %d is NULL", r);
+    if (limit_ns == 0) limit_ns = 2000000000ull;
+    CK(launch_shard_handshake(d_bufs, flag_offset, nranks, rank, epoch, limit_ns, d_error_flag,
+                              (cudaStream_t)stream));
     return QS_OK;
 }
 

@@ -20,7 +20,7 @@
 //   warps 2-5 read the accumulator with tcgen05.ld (each warp its 32 TMEM
 //           lanes = 32 batch rows), round to bf16 and store the logits:
 //           to [B, V], or, for a vocabulary-sharded launch, each row to the
-//           buffer of the GPU that samples it (peer stores over NVLink).
+//           buffer of the GPU that samples it (bulk copies over NVLink).
 // W is read from HBM exactly once per launch (311 MB for Qwen3-0.6B: the
 // bound); the hidden rows (at most 256 KB) are re-read from L2 per tile.
 // Every wait is bounded: after kLhWaitNs the kernel raises an error flag,
@@ -173,6 +173,9 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             int last_ph[kLhStages];
             for (int i = 0; i < kLhStages; i++) last_ph[i] = -1;
             bool stop = false;
+            // launched as a programmatic dependent of the RMSNorm kernel: the
+            // set-up above overlaps it; its rows are read only after it ends
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
                 for (int kb = 0; kb < nk; kb++) {
                     if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort, wait_ns)) { stop = true; break; }
@@ -232,10 +235,10 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // in shared memory and one lane stores them with a TMA bulk tensor
         // copy (whole row segments; rows past B and columns past V are
         // clipped by the copy).  In a sharded launch (peer.nranks > 0) the
-        // warp stages its rows the same way and then writes each row segment
-        // to the buffer of the rank that samples that row (this GPU's or a
-        // peer's over NVLink), 16 bytes per lane.  Otherwise each lane stores
-        // its own row.
+        // warp stages its rows the same way and each lane copies its row
+        // segment to the buffer of the rank that samples that row (this
+        // GPU's or a peer's over NVLink) with one bulk copy.  Otherwise each
+        // lane stores its own row.
         const bool staged = tma_out || peer.nranks > 0;
         const int q = warp & 3;
         const int row = q * 32 + lane;
@@ -249,6 +252,8 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc_fence_after();
             const int n0 = tile * kLhN;
             if (tma_out && lane == 0)  // the previous tile's store has read the staging rows
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            if (peer.nranks > 0)  // this lane's previous row copy has read its staging row
                 asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             __syncwarp();
             // the row's running segment maximum (order key) over this tile's
@@ -301,7 +306,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             if (run && row < B) atomicMax(segk + (size_t)row * segk_stride + rseg, run);
             tc_fence_before();
-            if (tma_out) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (staged) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&sh->tempty[b]);
@@ -315,24 +320,26 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
             }
             // (the accumulator is released above: its values are in the staging rows)
-            if (peer.nranks > 0) {
-                const uint4* rows = reinterpret_cast<const uint4*>(sC + q * kLhOutTile);
-                constexpr int kChunks = kLhN / 8;  // 16-byte pieces of a staged row
-                for (int rr = 0; rr < 32; rr++) {
-                    const int grow = peer.row0 + q * 32 + rr;
-                    if (q * 32 + rr >= B) break;
-                    const int rk = grow / peer.rows_per;
-                    uint4* drow = reinterpret_cast<uint4*>(peer.dst[rk] + (size_t)(grow - rk * peer.rows_per) * peer.ld +
-                                                           peer.col0 + n0);
-                    for (int c = lane; c < kChunks; c += 32)
-                        if (n0 + c * 8 < V) drow[c] = rows[rr * kChunks + c];
-                }
-                __syncwarp();
+            if (peer.nranks > 0 && row < B) {
+                // each lane's row segment to the rank that samples the row, as
+                // one bulk copy (over NVLink for a peer; 16-byte aligned: the
+                // host checks the buffers, col0 and the vocabulary)
+                const int grow = peer.row0 + row;
+                const int rk = grow / peer.rows_per;
+                const int ncols = min(kLhN, V - n0);
+                __nv_bfloat16* d = peer.dst[rk] + (size_t)(grow - rk * peer.rows_per) * peer.ld + peer.col0 + n0;
+                asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(d),
+                             "r"(smem_u32(stage)), "r"(ncols * 2)
+                             : "memory");
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             }
         }
         if (tma_out && lane == 0)  // the last stores complete before the CTA leaves
             asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-        if (peer.nranks > 0) __threadfence_system();  // peer stores visible before the kernel ends
+        if (peer.nranks > 0) {
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // this lane's row copies are done
+            __threadfence_system();  // and visible to the peers before the kernel ends
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -344,12 +351,53 @@ lm_head_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (threadIdx.x == 0 && *abort) atomicExch(err, 1);
 }
 
+// Completion handshake of a vocabulary-sharded launch, on the stream after
+// it: lane r publishes `epoch` into rank r's flag word for this rank
+// (release, system scope: this GPU's peer stores of the launch before it are
+// visible first), then waits until rank r's word in this rank's flags
+// reaches `epoch` (acquire).  The wait is bounded by limit_ns; then *err = 1
+// and the lane returns.  Flags: nranks words at byte offset flag_off of every
+// rank's buffer, word s written by rank s.
+struct ShardFlags {
+    unsigned char* base[kLhMaxRanks];
+};
+__global__ void shard_handshake_kernel(const __grid_constant__ ShardFlags f, size_t flag_off, int nranks,
+                                       int rank, unsigned epoch, unsigned long long limit_ns,
+                                       int* __restrict__ err) {
+    const int r = threadIdx.x;
+    if (r >= nranks) return;
+    __threadfence_system();
+    unsigned* dst = reinterpret_cast<unsigned*>(f.base[r] + flag_off) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(dst), "r"(epoch) : "memory");
+    const unsigned* mine = reinterpret_cast<const unsigned*>(f.base[rank] + flag_off) + r;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if ((int)(v - epoch) >= 0) break;
+        if (global_ns() - t0 > limit_ns) {
+            atomicExch(err, 1);
+            break;
+        }
+    }
+}
+
+cudaError_t launch_shard_handshake(void* const* bufs, size_t flag_off, int nranks, int rank, unsigned epoch,
+                                   unsigned long long limit_ns, int* err, cudaStream_t stream) {
+    ShardFlags f;
+    memset(&f, 0, sizeof(f));
+    for (int r = 0; r < nranks; r++) f.base[r] = static_cast<unsigned char*>(bufs[r]);
+    shard_handshake_kernel<<<1, 32, 0, stream>>>(f, flag_off, nranks, rank, epoch, limit_ns, err);
+    return cudaGetLastError();
+}
+
 // Restates rms_norm_kernel (qwen_model.cuh:125-177) for one row per CTA.
 constexpr int kNormThreads = 256;
 
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ w,
                     __nv_bfloat16* __restrict__ Y, int D, float inv_d, float eps) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the lm_head may start its set-up
     const int t = threadIdx.x;
     const int half = D / 2;
     const __nv_bfloat162* in = reinterpret_cast<const __nv_bfloat162*>(X + (size_t)blockIdx.x * D);
@@ -434,9 +482,21 @@ static cudaError_t lm_head_go(const CUtensorMap& ma, const __nv_bfloat16* W, __n
     const size_t smem = LhTile<N>::smem();
     cudaError_t e = cudaFuncSetAttribute(lm_head_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    lm_head_kernel<N><<<grid, kLhThreads, smem, stream>>>(ma, mb, mc, tma_out, logits, B, V, K, ntiles, err, peer,
-                                                            g_wait_ns, segk, segk_stride);
-    return cudaGetLastError();
+    // programmatic dependent launch: the kernel may start while the launch
+    // before it (the RMSNorm) runs, and waits for it before its first load
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kLhThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, lm_head_kernel<N>, ma, mb, mc, tma_out, logits, B, V, K, ntiles, err, peer,
+                              g_wait_ns, segk, segk_stride);
 }
 
 // The tile width whose tiles spread most evenly over num_sms persistent CTAs

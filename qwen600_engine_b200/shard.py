@@ -17,8 +17,10 @@ other way: splitting its rows would make every GPU stream the whole 311 MB
 weight, so ``VocabShardedLmHead`` splits the vocabulary (``vocab_shard``).
 Each GPU computes its slice of every row's logits and stores each row segment
 straight into the buffer of the GPU that samples that row (peer stores over
-NVLink inside the lm_head kernel); after one completion barrier every GPU
-holds whole rows of its ``row_block`` and samples them as above.
+NVLink inside the lm_head kernel).  A small kernel after it completes the
+call on the device (``qs_shard_handshake``): it publishes the call's epoch
+into every GPU's flag words and waits, bounded, for every GPU's; then each
+GPU holds whole rows of its ``row_block`` and samples them as above.
 """
 import ctypes as C
 from typing import List, Optional, Tuple
@@ -103,7 +105,10 @@ class VocabShardedLmHead:
     logit rows, bit-identical to the single-GPU ``lm_head``.  The row buffers
     are mapped between the processes once, at construction (CUDA IPC; every
     rank must construct and ``close`` together, since both exchange over the
-    process group)."""
+    process group).  Each call ends with the device-side handshake, so no
+    collective runs per call; every rank must have read its rows of one call
+    before any rank makes the next (in a decode loop the token exchange
+    between steps orders this)."""
 
     def __init__(self, weight_shard, col0: int, vocab: int, max_batch: int, *, rank: int, world: int,
                  group=None):
@@ -123,7 +128,9 @@ class VocabShardedLmHead:
         self.device = self.weight.device
         self.hidden_dim = int(self.weight.shape[1])
         self.rows_cap = -(-self.max_batch // world)
-        nbytes = self.rows_cap * self.vocab * 2
+        # the rows, then one 32-bit flag word per rank (written by that rank)
+        self.flag_off = -(-(self.rows_cap * self.vocab * 2) // 256) * 256
+        nbytes = self.flag_off + 256
         hb = self.lib.qs_ipc_handle_bytes()
         handle = (C.c_ubyte * hb)()
         own = C.c_void_p()
@@ -148,13 +155,13 @@ class VocabShardedLmHead:
         self.rows = _wrap_device(self._own, (self.rows_cap, self.vocab), torch.bfloat16, dev)
         self.normed = torch.empty((self.max_batch, self.hidden_dim), dtype=torch.bfloat16, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        self.wait_limit_ns = 2_000_000_000
 
     def __call__(self, hidden, norm_weight=None, stream=None, weight=None):
         """This rank's rows [start, stop) of ``row_block(rank, world, B)`` as a
         bf16 [stop - start, vocab] view of its row buffer (valid until the
         next call).  ``weight`` replaces the shard for this call (same shape)."""
-        import torch.distributed as dist
         from . import _lib
         from .sampler import _ptr, _stream_handle
         B = int(hidden.shape[0])
@@ -168,8 +175,11 @@ class VocabShardedLmHead:
                                              self.hidden_dim, self.vocab, self.col0, self.cols,
                                              _ptr(self.normed), self._dst, self.world, per,
                                              _ptr(self.err), _stream_handle(stream)))
-        # every rank's stores have landed once every rank's kernel is done
-        dist.all_reduce(self._flag, group=self.group)
+        # every rank's stores have landed once every rank has published this
+        # call's epoch (after its kernel) into this rank's flags
+        self.epoch = self.epoch % 0xFFFFFFFF + 1  # 1, 2, ..., never 0 (the words' initial value)
+        _lib.check(self.lib.qs_shard_handshake(self._dst, self.world, self.rank, self.flag_off, self.epoch,
+                                               self.wait_limit_ns, _ptr(self.err), _stream_handle(stream)))
         start, stop = row_block(self.rank, self.world, B)
         return self.rows[:stop - start]
 

@@ -1,9 +1,13 @@
-"""Vocabulary-sharded decode tail on two GPUs (one process each, NCCL):
-each rank computes its slice of every row's logits and stores row segments
-into the rank that samples the row (peer stores over NVLink inside the
-lm_head kernel).  Each rank's whole rows must equal the single-GPU lm_head's
-bit for bit, and sampling them must give the single-GPU tokens.  Needs two
-GPUs; skipped otherwise."""
+"""Vocabulary-sharded decode tail on two GPUs (one process each, NCCL for
+set-up only): each rank computes its slice of every row's logits and copies
+row segments into the rank that samples the row (bulk copies over NVLink
+inside the lm_head kernel), then the ranks complete the call with a
+device-side flag handshake.  Each rank's whole rows must equal the
+single-GPU lm_head's bit for bit, and sampling them must give the
+single-GPU tokens.  Needs two GPUs; skipped otherwise.  The handshake's own
+cases run on one GPU: a flag word already published passes at once, and a
+flag that nothing sets makes the bounded wait give up with the error flag
+raised."""
 import os
 import socket
 
@@ -80,3 +84,34 @@ def test_two_gpu_vocab_sharded_lm_head(tmp_path, B, V):
         got = np.load(out + f".{r}.npy")
         assert got[0] and got[1], f"rank {r}: rows differ from the single-GPU lm_head"
         assert got[2], f"rank {r}: tokens differ"
+
+
+def test_handshake_on_one_gpu():
+    """The handshake kernel against flag words set by the host (no second
+    kernel to wait for): with the peer's word already at the epoch the call
+    completes and leaves the error flag clear; with a word that nothing sets
+    the wait runs out after its limit and raises the error flag; the context
+    stays usable."""
+    import ctypes as C
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from qwen600_engine_b200 import _lib
+    lib = _lib.lib
+    bufs = [torch.zeros(64, dtype=torch.int32, device="cuda") for _ in range(2)]
+    ptrs = (C.c_void_p * 2)(*[b.data_ptr() for b in bufs])
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # rank 0 of 2; its own word 1 (rank 1's) already holds epoch 3
+    bufs[0][1] = 3
+    torch.cuda.synchronize()
+    _lib.check(lib.qs_shard_handshake(ptrs, 2, 0, 0, 3, 10_000_000, C.c_void_p(err.data_ptr()), None))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert int(bufs[0][0].item()) == 3 and int(bufs[1][0].item()) == 3  # published to both ranks
+    # epoch 4: rank 1's word stays at 3, so the wait gives up after 10 ms
+    _lib.check(lib.qs_shard_handshake(ptrs, 2, 0, 0, 4, 10_000_000, C.c_void_p(err.data_ptr()), None))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+    assert int(bufs[1][0].item()) == 4
+    x = torch.arange(10, device="cuda").sum()
+    assert int(x.item()) == 45
