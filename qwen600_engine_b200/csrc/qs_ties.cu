@@ -93,12 +93,23 @@ __device__ __forceinline__ int tie_cta_sum(int v, int* red) {
 // Array accessors: keys (order keys of t) and element indices in separate
 // arrays.  Global scratch is shared by the cluster's CTAs on different SMs,
 // so it bypasses L1 (ld/st .cg); shared memory is plain.
+// The row's arrangement in L2-resident scratch: one 8-byte element per
+// position, (index << 32) | key, so a swap moves each element with one
+// access (the swaps' positions are scattered: one sector per element).
 struct GlobalArr {
-    uint32_t* k;
-    int* idx;
-    __device__ __forceinline__ uint32_t key(int q) const { return __ldcg(k + q); }
-    __device__ __forceinline__ int index(int q) const { return __ldcg(idx + q); }
-    __device__ __forceinline__ void put(int q, uint32_t kv, int iv) const { __stcg(k + q, kv); __stcg(idx + q, iv); }
+    unsigned long long* kv;
+    __device__ __forceinline__ uint32_t key(int q) const {
+        return __ldcg(reinterpret_cast<const uint32_t*>(kv + q));
+    }
+    __device__ __forceinline__ int index(int q) const { return (int)(__ldcg(kv + q) >> 32); }
+    __device__ __forceinline__ unsigned long long get(int q) const { return __ldcg(kv + q); }
+    __device__ __forceinline__ void set(int q, unsigned long long e) const { __stcg(kv + q, e); }
+    __device__ __forceinline__ void put(int q, uint32_t k, int i) const {
+        set(q, ((unsigned long long)(uint32_t)i << 32) | k);
+    }
+    __device__ __forceinline__ void set_index(int q, int i) const {
+        __stcg(reinterpret_cast<int*>(kv + q) + 1, i);
+    }
 };
 struct SharedArr {
     uint32_t* k;  // indexed by position - offset
@@ -106,6 +117,13 @@ struct SharedArr {
     __device__ __forceinline__ uint32_t key(int q) const { return k[q]; }
     __device__ __forceinline__ int index(int q) const { return idx[q]; }
     __device__ __forceinline__ void put(int q, uint32_t kv, int iv) const { k[q] = kv; idx[q] = iv; }
+    __device__ __forceinline__ unsigned long long get(int q) const {
+        return ((unsigned long long)(uint32_t)idx[q] << 32) | k[q];
+    }
+    __device__ __forceinline__ void set(int q, unsigned long long e) const {
+        k[q] = (uint32_t)e;
+        idx[q] = (int)(e >> 32);
+    }
 };
 struct GlobalPos {
     int* p;
@@ -283,8 +301,8 @@ template <class Arr, class Pos>
 __device__ __forceinline__ void do_swaps(const Arr& A, const Pos& posL, const Pos& posR, int T, int t0,
                                          int stride) {
     for (int tb = t0; tb < T; tb += 4 * stride) {
-        int x[4], y[4], ix[4], iy[4];
-        uint32_t kx[4], ky[4];
+        int x[4], y[4];
+        unsigned long long ex[4], ey[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const int t = tb + u * stride;
@@ -294,12 +312,12 @@ __device__ __forceinline__ void do_swaps(const Arr& A, const Pos& posL, const Po
 #pragma unroll
         for (int u = 0; u < 4; u++)
             if (x[u] >= 0 && x[u] != y[u]) {
-                kx[u] = A.key(x[u]); ix[u] = A.index(x[u]);
-                ky[u] = A.key(y[u]); iy[u] = A.index(y[u]);
+                ex[u] = A.get(x[u]);
+                ey[u] = A.get(y[u]);
             }
 #pragma unroll
         for (int u = 0; u < 4; u++)
-            if (x[u] >= 0 && x[u] != y[u]) { A.put(x[u], ky[u], iy[u]); A.put(y[u], kx[u], ix[u]); }
+            if (x[u] >= 0 && x[u] != y[u]) { A.set(x[u], ey[u]); A.set(y[u], ex[u]); }
     }
 }
 
@@ -493,21 +511,24 @@ __host__ __device__ __forceinline__ int tie_mask_words(int V) {
 // (sampler.h:197-206) as sort keys beside their indices, the stable sort of
 // the k by probability, descending (sampler.h:214; equal probabilities keep
 // position order, as glibc's stable qsort leaves them), then min-p / top-p /
-// renormalise / draw (sampler.h:144-162, 220-254).  The keys go to the row's
-// key array, the indices stay in place; the position arrays are the sort's
+// renormalise / draw (sampler.h:144-162, 220-254).  Keys and indices go to
+// the position arrays (kA, iA); the arrangement's words are the sort's
 // second buffer.  stg: kTieStage floats of shared memory (the passes'
 // histogram, then the serial walks' staging).
 constexpr int kTieStage = 4 * kTieSmemRange;
 template <typename T>
-__device__ __noinline__ void tie_draw_large(const T* __restrict__ L, int k, const GlobalArr& A, uint32_t* kB,
-                                            uint32_t* iB, const int* ovi, const float* ovv, int nov,
-                                            const RowResult& rr, const TieParams& prm, const ExpFix& fx,
-                                            float* stg, uint32_t* red, RowResult* res, int row,
-                                            int* cand_index_out, float* cand_prob_out, int cand_cap) {
-    uint32_t* kA = A.k;
-    uint32_t* iA = reinterpret_cast<uint32_t*>(A.idx);
+__device__ __noinline__ void tie_draw_large(const T* __restrict__ L, int k, int V, const GlobalArr& A,
+                                            uint32_t* kA, uint32_t* iA, const int* ovi, const float* ovv,
+                                            int nov, const RowResult& rr, const TieParams& prm,
+                                            const ExpFix& fx, float* stg, uint32_t* red, RowResult* res,
+                                            int row, int* cand_index_out, float* cand_prob_out, int cand_cap) {
+    // the sort's second buffers: the arrangement's own words, free once the
+    // indices are copied out
+    uint32_t* kB = reinterpret_cast<uint32_t*>(A.kv);
+    uint32_t* iB = kB + V;
     for (int q = threadIdx.x; q < k; q += kTieThreads) {
         const int t = A.index(q);
+        __stcg(iA + q, (uint32_t)t);
         float l = Elem<T>::widen(L[t]);
         int a = 0, b = nov;  // the override of t, if any (ovi ascending)
         while (a < b) { const int m = (a + b) >> 1; if (ovi[m] < t) a = m + 1; else b = m; }
@@ -562,8 +583,7 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
     const int cid = blockIdx.x / kTieCluster;
     const int ncl = gridDim.x / kTieCluster;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const GlobalArr A{reinterpret_cast<uint32_t*>(scratch + (size_t)cid * V),
-                      reinterpret_cast<int*>(scratch + (size_t)cid * V) + V};
+    const GlobalArr A{scratch + (size_t)cid * V};
     const GlobalPos gposL{pos_scratch + (size_t)cid * 2 * V};
     const GlobalPos gposR{pos_scratch + (size_t)cid * 2 * V + V};
     const int nslow = *slow_count;
@@ -669,14 +689,14 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
         // land after the first CTA's writes)
         if (!more && k <= kTieSortCap && lo >= 0 && lo <= hi && hi < V) {
             // After the cluster's last row only the first CTA reads the
-            // scratch again, and only keys [lo, hi] and indices [0, max(k, hi + 1)):
-            // every CTA drops its share of the rest from L2 (the position
-            // arrays entirely) while the first continues.
+            // scratch again, and only elements [0, max(k, hi + 1)) (keys
+            // [lo, hi], indices [0, k)): every CTA drops its share of the
+            // rest from L2 (the position arrays entirely) while the first
+            // continues.
             const int idx_keep = max(k, hi + 1);
-            discard_l2_part(A.k, sizeof(uint32_t) * (size_t)lo, crank, kTieCluster);
-            discard_l2_part(A.k + hi + 1, sizeof(uint32_t) * (size_t)(V - 1 - hi), crank, kTieCluster);
             if (idx_keep < V)
-                discard_l2_part(A.idx + idx_keep, sizeof(int) * (size_t)(V - idx_keep), crank, kTieCluster);
+                discard_l2_part(A.kv + idx_keep, sizeof(unsigned long long) * (size_t)(V - idx_keep), crank,
+                                kTieCluster);
             discard_l2_part(gposL.p, sizeof(int) * 2 * (size_t)V, crank, kTieCluster);
         }
         if (!more && crank != 0) return;
@@ -719,12 +739,12 @@ ties_kernel(const T* __restrict__ logits, int V, TieParams prm, const int* __res
                 }
                 __syncthreads();
                 // the range's final arrangement (indices; the keys are not read again)
-                for (int q = tid; q < wn; q += kTieThreads) __stcg(A.idx + woff + q, sI[q]);
+                for (int q = tid; q < wn; q += kTieThreads) A.set_index(woff + q, sI[q]);
                 __syncthreads();
             }
             if (ph && tid == 0) { ph[3] = clock64(); ph[7] = rounds; }
             if (k > kTieSortCap) {
-                tie_draw_large<T>(L, k, A, reinterpret_cast<uint32_t*>(gposL.p),
+                tie_draw_large<T>(L, k, V, A, reinterpret_cast<uint32_t*>(gposL.p),
                                   reinterpret_cast<uint32_t*>(gposR.p), ovi, ovv, nov, rr, prm, fx,
                                   reinterpret_cast<float*>(sK), reinterpret_cast<uint32_t*>(red), res, row,
                                   cand_index_out, cand_prob_out, cand_cap);
