@@ -557,65 +557,94 @@ def main():
     toks = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
     glist = [[torch.empty(B, dtype=torch.int32, device=dev) for _ in range(world)]
              for _ in range(2)] if (world > 1 and rank == 0) else [None, None]
-    s = Sampler(PARAMS["temperature"], PARAMS["topp"], PARAMS["minp"], PARAMS["top_k"],
-                PARAMS["repetition_penalty"], PARAMS["frequency_penalty"],
-                PARAMS["presence_penalty"], WINDOW, 1, max_batch=B, vocab=V, device=local)
+    # two independent batches in flight, each with its own handle (scratch)
+    # and stream: batch i runs on handle/stream i % 2, so one batch's
+    # latency-bound passes (finishing, tie replay) overlap the next batch's
+    # HBM-bound streaming pass.  The one-batch-at-a-time latency is measured
+    # too (handle 0 alone on the launching stream).
+    ss = [Sampler(PARAMS["temperature"], PARAMS["topp"], PARAMS["minp"], PARAMS["top_k"],
+                  PARAMS["repetition_penalty"], PARAMS["frequency_penalty"],
+                  PARAMS["presence_penalty"], WINDOW, 1, max_batch=B, vocab=V, device=local)
+          for _ in range(2)]
+    s = ss[0]
     main_stream = torch.cuda.current_stream()
+    streams = [main_stream, torch.cuda.Stream()]
+    rngs = [rng, rng.clone()]
     gstream = torch.cuda.Stream() if world > 1 else None
     gdone = [torch.cuda.Event(), torch.cuda.Event()]
 
-    def step(i):
+    def step(i, nflight=2):
         j = i % 2
+        k = i % nflight
+        st = streams[k]
         if world > 1 and i >= 2:
-            main_stream.wait_event(gdone[j])
-        s.sample_rows(bufs[j][0], hist, counts, count, rng, out=toks[j])
+            st.wait_event(gdone[j])
+        with torch.cuda.stream(st):
+            ss[k].sample_rows(bufs[j][0], hist, counts, count, rngs[k], out=toks[j], stream=st)
         if world > 1:
             ev = torch.cuda.Event()
-            ev.record(main_stream)
+            ev.record(st)
             with torch.cuda.stream(gstream):
                 gstream.wait_event(ev)
                 dist.gather(toks[j], gather_list=glist[j], dst=0)
                 gdone[j].record(gstream)
 
-    def sync_all():
+    def join():
+        for st in streams[1:]:
+            main_stream.wait_stream(st)
         if gstream is not None:
             main_stream.wait_stream(gstream)
+
+    def sync_all():
+        join()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
     rng_init = rng.clone()
-    for i in range(args.warmup):
+    for i in range(max(args.warmup, 2)):
         step(i)
     sync_all()
 
-    # ---- timed region (device time, launching stream)
-    prof0 = s.profile_read()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    def timed(nflight):
+        # device time on the launching stream; the other stream starts after t0
+        # and the launching stream waits for it before t1
+        p0 = [h.profile_read()["launches"] for h in ss]
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
         t0.record(main_stream)
+        for st in streams[1:]:
+            st.wait_stream(main_stream)
         for i in range(args.steps):
-            step(i)
-        if gstream is not None:
-            main_stream.wait_stream(gstream)
+            step(i, nflight)
+        join()
         t1.record(main_stream)
         torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1)
-    prof1 = s.profile_read()
-    launches = int(prof1["launches"] - prof0["launches"])
+        nl = sum(int(h.profile_read()["launches"] - a) for h, a in zip(ss, p0))
+        return t0.elapsed_time(t1), nl
+
+    # ---- one batch at a time (latency per batch)
+    ms1, _ = timed(1)
+    sync_all()
+    if world > 1:
+        ms1 = shard.max_over_ranks(ms1, device=dev)
+    latency_ms = ms1 / args.steps
+    # ---- timed region: two batches in flight (throughput)
+    with ClockSampler(local) as clk:
+        ms, launches = timed(2)
     sync_all()
     if world > 1:
         ms = shard.max_over_ranks(ms, device=dev)
     ms_step = ms / args.steps
     value = world * B / (ms_step / 1e3)
 
-    # ---- per-kernel timing of the same steps (separate pass, events around each kernel)
+    # ---- per-kernel timing of the same steps (separate pass, one batch at a
+    # time on handle 0, events around each kernel)
     s.profile(True)
     s.profile_reset()
     for i in range(args.steps):
-        step(i)
+        step(i, 1)
     sync_all()
     pr = s.profile_read()
     s.profile(False)
@@ -708,11 +737,14 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "batches_in_flight": 2, "latency_ms_per_batch": latency_ms,
+        "rows_per_s_one_batch_in_flight": world * B / (latency_ms / 1e3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "global_batch": world * B, "rows_per_gpu": B,
                    "vocab": V, "window": WINDOW, "seq_len": None,
-                   "parallelism": f"row-sharded x{world}, tokens gathered to rank 0",
+                   "parallelism": f"row-sharded x{world}, tokens gathered to rank 0; per GPU two independent "
+                                  "batches in flight (two handles, two streams)",
                    "l2": "inputs larger than L2: two 311 MB logit buffers used in turn"},
         "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": step_ach, "peak": hbm, "unit": "GB/s",
@@ -732,7 +764,8 @@ def main():
         "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)
-    s.free()
+    for h in ss:
+        h.free()
     return 0
 
 
