@@ -283,6 +283,13 @@ QS_API int qs_lm_head_shard(const void* d_hidden, const void* d_norm_weight, con
 QS_API int qs_shard_handshake(void* const* d_bufs, int nranks, int rank, size_t flag_offset, unsigned epoch,
                               unsigned long long limit_ns, int* d_error_flag, void* stream);
 
+/* One device-to-device copy of `bytes` on `stream`; either pointer may be a
+ * peer's buffer mapped with qs_ipc_open (the copy then crosses NVLink).  The
+ * token gather of the row-sharded sampling path uses it to write each rank's
+ * tokens into rank 0's buffer before qs_shard_handshake.  No counterpart in
+ * the reference (which runs on one GPU). */
+QS_API int qs_copy_async(void* d_dst, const void* d_src, size_t bytes, void* stream);
+
 QS_API int qs_ipc_handle_bytes(void);
 QS_API int qs_ipc_alloc(size_t bytes, void** d_ptr, void* handle);
 QS_API int qs_ipc_open(const void* handle, void** d_ptr);

@@ -33,7 +33,7 @@ EXPORTS = (
     "qs_profile_phases", "qs_profile_phases_read",
     "qs_argmax_rows_static", "qs_lm_head", "qs_lm_head_sample", "qs_lm_head_logits",
     "qs_lm_head_status", "qs_lm_head_set_wait_limit", "qs_lm_head_shard", "qs_ipc_handle_bytes", "qs_ipc_alloc", "qs_ipc_open",
-    "qs_ipc_close", "qs_ipc_free", "qs_shard_handshake",
+    "qs_ipc_close", "qs_ipc_free", "qs_shard_handshake", "qs_copy_async",
 )
 
 
@@ -106,6 +106,7 @@ def _load() -> C.CDLL:
     lib.qs_ipc_close.argtypes = [vp]
     lib.qs_ipc_free.argtypes = [vp]
     lib.qs_shard_handshake.argtypes = [P(vp), i32, i32, C.c_size_t, u32, C.c_ulonglong, vp, vp]
+    lib.qs_copy_async.argtypes = [vp, vp, C.c_size_t, vp]
     lib.qs_last_error.restype = C.c_char_p
     lib.qs_last_error.argtypes = []
     lib.qs_max_vocab.argtypes = []

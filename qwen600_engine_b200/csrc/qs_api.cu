@@ -943,6 +943,14 @@ int qs_ipc_free(void* d_ptr) {
     return QS_OK;
 }
 
+int qs_copy_async(void* d_dst, const void* d_src, size_t bytes, void* stream) {
+    g_err.clear();
+    if (bytes == 0) return QS_OK;
+    if (!d_dst || !d_src) return fail(QS_ERR_INVALID, "NULL pointer");
+    CK(cudaMemcpyAsync(d_dst, d_src, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+    return QS_OK;
+}
+
 int qs_shard_handshake(void* const* d_bufs, int nranks, int rank, size_t flag_offset, unsigned epoch,
                        unsigned long long limit_ns, int* d_error_flag, void* stream) {
     g_err.clear();

@@ -5,8 +5,10 @@ sequence, sampler.h:165, and ``sample()`` touches nothing else), so a batch
 splits into contiguous row blocks with no exchange while sampling.  Row r
 keeps the RNG stream it has on one GPU (seed + r, counted over the whole
 batch), so the sharded job draws exactly what the single-GPU job draws.  The
-only collective is the gather of the int32 tokens (and, when asked, the RNG
-states) to one rank, plus the max-over-ranks of the timed region.
+tokens go to one rank either with a collective (``gather_rows``, any
+per-row tensor) or with no collective at all (``TokenGather``: peer copies
+into rank 0's buffer and a device-side flag handshake), plus the
+max-over-ranks of the timed region.
 
 The functions take a torch.distributed process group (NCCL on GPUs, gloo in
 the CPU tests) and plain tensors; nothing above ``VocabShardedLmHead``
@@ -70,6 +72,100 @@ def gather_rows(local, batch: int, world: int, rank: int, dst: int = 0, group=No
         a, b = row_block(r, world, batch)
         out.append(parts[r][:b - a])
     return torch.cat(out, dim=0)
+
+
+class TokenGather:
+    """Gathers every rank's int32 tokens (its ``row_block``) to rank 0 without
+    a collective: each rank copies its block straight into rank 0's buffer
+    (device memory mapped through CUDA IPC; over NVLink), then the ranks run
+    the device-side flag handshake (``qs_shard_handshake``, bounded: a rank
+    that never arrives raises the error flag instead of hanging the others).
+    Two buffer slots alternate, so a call's tokens stay readable on rank 0
+    until the call after next.  The buffers are mapped once, at
+    construction; every rank must construct and ``close`` together."""
+
+    def __init__(self, batch: int, *, rank: int, world: int, device, group=None):
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+        from .sampler import _wrap_device
+        if world > 8:
+            raise ValueError("at most 8 ranks")
+        self.lib = _lib.lib
+        self.batch, self.rank, self.world, self.group = int(batch), rank, world, group
+        self.per = max(1, -(-self.batch // world))
+        self.device = torch.device(device)
+        dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        slot = world * self.per * 4
+        self.flag_off = -(-(2 * slot) // 256) * 256
+        hb = self.lib.qs_ipc_handle_bytes()
+        handle = (C.c_ubyte * hb)()
+        own = C.c_void_p()
+        _lib.check(self.lib.qs_ipc_alloc(self.flag_off + 256, C.byref(own), handle))
+        self._own = own.value
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        parts = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine, group=group)
+        ptrs, self._peers = [], []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self._own)
+                continue
+            h = (C.c_ubyte * hb).from_buffer_copy(bytes(parts[r].cpu().tolist()))
+            q = C.c_void_p()
+            _lib.check(self.lib.qs_ipc_open(h, C.byref(q)))
+            self._peers.append(q.value)
+            ptrs.append(q.value)
+        self._bufs = (C.c_void_p * world)(*ptrs)
+        self._root = ptrs[0]  # rank 0's two slots as seen from this rank (a peer mapping elsewhere)
+        self._view = _wrap_device(self._own, (2, world * self.per), torch.int32, dev) if rank == 0 else None
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        self.calls = 0
+        self.wait_limit_ns = 2_000_000_000
+
+    def __call__(self, tokens, stream=None):
+        """Copies this rank's tokens into rank 0's current slot and completes
+        the call; rank 0 gets the whole batch's tokens (a view of that slot,
+        valid for the next call as well), other ranks None."""
+        import torch
+        from . import _lib
+        from .sampler import _ptr, _stream_handle
+        a, b = row_block(self.rank, self.world, self.batch)
+        if tokens.shape[0] != b - a:
+            raise ValueError(f"rank {self.rank} holds {tokens.shape[0]} rows, its block has {b - a}")
+        j = self.calls % 2
+        self.calls += 1
+        if b > a:
+            if not tokens.is_contiguous() or tokens.dtype != torch.int32:
+                raise ValueError("tokens must be a contiguous int32 CUDA tensor")
+            dst = self._root + (j * self.world * self.per + a) * 4
+            _lib.check(self.lib.qs_copy_async(C.c_void_p(dst), _ptr(tokens), (b - a) * 4,
+                                              _stream_handle(stream)))
+        self.epoch = self.epoch % 0xFFFFFFFF + 1
+        _lib.check(self.lib.qs_shard_handshake(self._bufs, self.world, self.rank, self.flag_off, self.epoch,
+                                               self.wait_limit_ns, _ptr(self.err), _stream_handle(stream)))
+        return self._view[j, :self.batch] if self.rank == 0 else None
+
+    def status(self) -> None:
+        """Raises if a handshake gave up waiting for a rank."""
+        from . import _lib
+        if int(self.err.item()) != 0:
+            raise _lib.SamplerError(_lib.QS_ERR_CUDA, "token gather: a rank did not arrive in time")
+
+    def close(self) -> None:
+        import torch
+        import torch.distributed as dist
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self._view = None
+        for p in self._peers:
+            self.lib.qs_ipc_close(C.c_void_p(p))
+        self._peers = []
+        dist.barrier(group=self.group)
+        self.lib.qs_ipc_free(C.c_void_p(self._own))
+        self._own = None
 
 
 def max_over_ranks(value: float, device=None, group=None) -> float:

@@ -86,6 +86,53 @@ def test_two_gpu_vocab_sharded_lm_head(tmp_path, B, V):
         assert got[2], f"rank {r}: tokens differ"
 
 
+def _gather_main(rank, world, port, B, out_path):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from qwen600_engine_b200 import shard
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    tg = None
+    try:
+        dev = torch.device("cuda", rank)
+        tg = shard.TokenGather(B, rank=rank, world=world, device=dev)
+        a, b = shard.row_block(rank, world, B)
+        ok = []
+        for call in range(3):  # both slots, then the first again
+            toks = (torch.arange(a, b, dtype=torch.int32, device=dev) * 7 + 1000 * call)
+            got = tg(toks)
+            want = shard.gather_rows(toks, B, world, rank)  # NCCL (blocks padded to a common length)
+            torch.cuda.synchronize()
+            if rank == 0:
+                ok.append(bool(torch.equal(got, want)))
+        tg.status()
+        np.save(out_path + f".{rank}.npy", np.array(ok if rank == 0 else [True]))
+    finally:
+        if tg is not None:
+            tg.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("B", [2048, 101])
+def test_two_gpu_token_gather_without_collective(tmp_path, B):
+    """shard.TokenGather: each rank copies its tokens into rank 0's buffer
+    over NVLink and the device handshake completes the call; rank 0's result
+    equals NCCL's gather, on three calls in a row (both buffer slots)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "g")
+    mp.start_processes(_gather_main, args=(2, _free_port(), B, out), nprocs=2, start_method="spawn")
+    assert np.load(out + ".0.npy").all(), "gathered tokens differ from NCCL's gather"
+    assert np.load(out + ".1.npy").all()
+
+
 def test_handshake_on_one_gpu():
     """The handshake kernel against flag words set by the host (no second
     kernel to wait for): with the peer's word already at the epoch the call
